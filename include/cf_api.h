@@ -1,0 +1,119 @@
+/*
+ * cudaforge_b200 C ABI -- the drop-in boundary of the speculative-decoding
+ * verify + accept path on B200 (sm_100a).
+ *
+ * Conventions (all entry points):
+ *   - plain pointers, sizes and POD argument structs; no C++ or torch types;
+ *   - every device pointer is caller-owned; the library allocates no device
+ *     memory of its own on these paths (scratch comes in through `workspace`
+ *     arguments sized by the matching *_workspace_bytes query);
+ *   - work is enqueued on the caller's stream (`stream` is a cudaStream_t;
+ *     NULL = legacy default stream) and the call returns without
+ *     synchronising;
+ *   - the return value is CF_OK (0) or a negative cf_status; nothing throws
+ *     across this boundary.  Argument errors are detected on the host before
+ *     any launch; errors that depend on device data (an out-of-range draft
+ *     token, a block id outside the pool) are reported through the outputs
+ *     documented per call.
+ *
+ * The reference (CUDAForge) has no C ABI for this path; each entry point
+ * names the reference interface it replaces.
+ */
+#ifndef CF_API_H_
+#define CF_API_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum cf_status {
+  CF_OK = 0,
+  CF_EINVAL = -1,       /* bad argument (shape, null pointer, alignment)      */
+  CF_ERANGE = -2,       /* index out of range (block id, token id, sequence)  */
+  CF_ETIMEOUT = -3,     /* a bounded device-side wait gave up                  */
+  CF_ECUDA = -4,        /* a CUDA runtime call failed                          */
+  CF_ENOMEM = -5,       /* host allocation failed / KV pool exhausted          */
+  CF_EUNSUPPORTED = -6  /* configuration not built in this library            */
+} cf_status;
+
+typedef enum cf_dtype {
+  CF_F32 = 0,
+  CF_BF16 = 1,
+  CF_F16 = 2
+} cf_dtype;
+
+/* Human-readable name of a status code (static storage). */
+const char *cf_status_string(int status);
+
+/* Library version string, e.g. "cudaforge_b200 0.1 sm_100a". */
+const char *cf_version(void);
+
+/* ------------------------------------------------------------------------
+ * Acceptance sampling
+ *
+ * Replaces: SpeculativeEngine::verify_candidates and
+ * SpeculativeEngine::verify_candidates_greedy
+ * (csrc/include/cudaforge/scheduler/speculative.h:48-63,
+ *  csrc/src/scheduler/speculative.cpp:50-150, bound in
+ *  csrc/bindings/pybind_module.cpp:229-236), batched over sequences and fed
+ * logits instead of probability lists.  The softmax of
+ * cudaforge/speculative.py:118 and :145 (softmax(logits / T)) is fused in.
+ *
+ * Per sequence b (K = k):
+ *   q = softmax(draft_logits[b, i] / T), p = softmax(target_logits[b, i] / T)
+ *   for i < K: ratio = q[x_i] > 0 ? min(1, p[x_i] / q[x_i]) : 0,
+ *              accept iff uniforms[b, i] <= ratio;
+ *              an accepted EOS stops with final token = EOS;
+ *              on the first rejection at i the final token is drawn from
+ *              norm(max(0, p - q)) (target row i when that sum <= 1e-6) with
+ *              uniforms[b, i + 1];
+ *   all accepted: the bonus token is drawn from p (target row K) with
+ *              uniforms[b, K].
+ * Draws are inverse-CDF with a sequential fp32 cumulative sum (first index
+ * with u <= cum, else V-1), exactly as the reference computes it.
+ * Greedy mode (greedy != 0): accept while x_i == argmax(p_i) (lowest index
+ * on ties), final = that argmax, bonus = argmax of row K; uniforms unused.
+ *
+ * Outputs: out_tokens[b, 0..n-1] = accepted drafts, out_tokens[b, n] = final
+ * token, n = out_num_accepted[b]; out_eos[b] = 1 when the sequence ended.
+ * A draft token outside [0, vocab) makes that sequence's out_num_accepted
+ * -1 (the reference's behaviour there is undefined).
+ *
+ * Optional parity export: when probs_draft / probs_target are non-NULL the
+ * kernel also writes the fp32 probabilities it decided on
+ * ([B, K, V] and [B, K+1, V], contiguous).
+ * ---------------------------------------------------------------------- */
+typedef struct cf_accept_args {
+  int32_t batch;            /* B >= 0                                   */
+  int32_t k;                /* K >= 0 draft tokens per sequence           */
+  int64_t vocab;            /* V >= 1                                   */
+  int32_t logits_dtype;     /* cf_dtype of both logits tensors          */
+  const void *draft_logits; /* row (b, i) at b*draft_seq_stride + i*draft_row_stride (elements) */
+  int64_t draft_seq_stride;
+  int64_t draft_row_stride;
+  const void *target_logits; /* row (b, i), i <= K                       */
+  int64_t target_seq_stride;
+  int64_t target_row_stride;
+  const int32_t *draft_tokens; /* [B, K] contiguous                      */
+  const float *uniforms;       /* [B, K+1] contiguous, U[0,1); NULL if greedy */
+  float temperature;           /* > 0 (the Python layer clamps at 1e-5)  */
+  int32_t eos_token_id;        /* -1: none                               */
+  int32_t greedy;
+  int32_t *out_tokens;       /* [B, K+1]                                 */
+  int32_t *out_num_accepted; /* [B]                                      */
+  uint8_t *out_eos;          /* [B]                                      */
+  void *workspace;           /* >= cf_accept_workspace_bytes(B, K) bytes, 16-B aligned */
+  float *probs_draft;        /* optional parity export                   */
+  float *probs_target;       /* optional parity export                   */
+} cf_accept_args;
+
+size_t cf_accept_workspace_bytes(int32_t batch, int32_t k);
+int cf_accept_sample(const cf_accept_args *args, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CF_API_H_ */

@@ -1,0 +1,138 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes front end to the CPU oracle.
+
+`liboracle.so` is this repository's C restatement of the reference acceptance
+algorithm (CUDAForge csrc/src/scheduler/speculative.cpp:12-150).
+`_ref/libspec_ref.so` is the unmodified reference code compiled from its own
+sources.  Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline /
+reference arm may import this package; the product path never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_P = ctypes.c_void_p
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _load(path):
+    if not os.path.exists(path):
+        build()
+    return ctypes.CDLL(path)
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        _lib = _load(os.path.join(HERE, "liboracle.so"))
+    return _lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(os.path.join(HERE, "_ref", "libspec_ref.so"))
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        _ref = ctypes.CDLL(os.path.join(HERE, "_ref", "libspec_ref.so"))
+    return _ref
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(_P)
+
+
+def accept(draft_tokens, draft_probs, target_probs, uniforms, eos):
+    """Batched restatement.  draft_tokens [B,K] int32, draft_probs [B,K,V] f32,
+    target_probs [B,K+1,V] f32, uniforms [B,K+1] f32.
+    Returns (tokens [B,K+1] int32, num_accepted [B] int32, eos [B] uint8)."""
+    dt = np.ascontiguousarray(draft_tokens, dtype=np.int32)
+    dp = np.ascontiguousarray(draft_probs, dtype=np.float32)
+    tp = np.ascontiguousarray(target_probs, dtype=np.float32)
+    u = np.ascontiguousarray(uniforms, dtype=np.float32)
+    B, K = dt.shape
+    V = tp.shape[-1]
+    tok = np.full((B, K + 1), -1, np.int32)
+    na = np.zeros(B, np.int32)
+    ef = np.zeros(B, np.uint8)
+    rc = lib().oref_accept_batch(ctypes.c_int32(B), ctypes.c_int32(K), ctypes.c_int64(V),
+                                 _ptr(dt), _ptr(dp), _ptr(tp), ctypes.c_int32(eos), _ptr(u),
+                                 _ptr(tok), _ptr(na), _ptr(ef))
+    assert rc == 0
+    return tok, na, ef
+
+
+def accept_greedy(draft_tokens, target_probs, eos):
+    dt = np.ascontiguousarray(draft_tokens, dtype=np.int32)
+    tp = np.ascontiguousarray(target_probs, dtype=np.float32)
+    B, K = dt.shape
+    V = tp.shape[-1]
+    tok = np.full((B, K + 1), -1, np.int32)
+    na = np.zeros(B, np.int32)
+    ef = np.zeros(B, np.uint8)
+    lib().oref_accept_greedy_batch(ctypes.c_int32(B), ctypes.c_int32(K), ctypes.c_int64(V),
+                                   _ptr(dt), _ptr(tp), ctypes.c_int32(eos),
+                                   _ptr(tok), _ptr(na), _ptr(ef))
+    return tok, na, ef
+
+
+def softmax_rows(x: np.ndarray, T: float) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    V = x.shape[-1]
+    flat_x = x.reshape(-1, V)
+    flat_o = out.reshape(-1, V)
+    for i in range(flat_x.shape[0]):
+        lib().oref_softmax_row(_ptr(flat_x[i]), ctypes.c_int64(V), ctypes.c_float(T), _ptr(flat_o[i]))
+    return out
+
+
+# ---- the unmodified reference (compiled) --------------------------------
+
+def ref_uniforms(seed: int, n: int) -> np.ndarray:
+    out = np.zeros(n, np.float32)
+    ref().ref_uniforms(ctypes.c_uint64(seed), ctypes.c_int32(n), _ptr(out))
+    return out
+
+
+def ref_verify(seed, draft_tokens, draft_probs, target_probs, eos):
+    """One sequence through SpeculativeEngine(rng_seed=seed).verify_candidates."""
+    dt = np.ascontiguousarray(draft_tokens, dtype=np.int32)
+    dp = np.ascontiguousarray(draft_probs, dtype=np.float32)
+    tp = np.ascontiguousarray(target_probs, dtype=np.float32)
+    K = dt.shape[0]
+    V = tp.shape[-1]
+    tok = np.full(K + 1, -1, np.int32)
+    na = np.zeros(1, np.int32)
+    ef = np.zeros(1, np.uint8)
+    rc = ref().ref_verify(ctypes.c_uint64(seed), ctypes.c_int32(K), ctypes.c_int64(V),
+                          _ptr(dt), _ptr(dp), _ptr(tp), ctypes.c_int32(eos),
+                          _ptr(tok), _ptr(na), _ptr(ef))
+    if rc != 0:
+        raise ValueError("reference verify_candidates raised")
+    return tok, int(na[0]), int(ef[0])
+
+
+def ref_verify_greedy(draft_tokens, target_probs, eos):
+    dt = np.ascontiguousarray(draft_tokens, dtype=np.int32)
+    tp = np.ascontiguousarray(target_probs, dtype=np.float32)
+    K = dt.shape[0]
+    V = tp.shape[-1]
+    tok = np.full(K + 1, -1, np.int32)
+    na = np.zeros(1, np.int32)
+    ef = np.zeros(1, np.uint8)
+    ref().ref_verify_greedy(ctypes.c_int32(K), ctypes.c_int64(V), _ptr(dt), _ptr(tp),
+                            ctypes.c_int32(eos), _ptr(tok), _ptr(na), _ptr(ef))
+    return tok, int(na[0]), int(ef[0])
