@@ -35,6 +35,15 @@ class CfAcceptArgs(ctypes.Structure):
     ]
 
 
+class CfGemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("m", _I32), ("n", _I32), ("k", _I32), ("act_dtype", _I32),
+        ("x", _P), ("ldx", _I64), ("w", _P), ("scales", _P), ("y", _P), ("ldy", _I64),
+        ("residual", _P), ("ldr", _I64), ("split_k", _I32), ("workspace", _P),
+        ("workspace_bytes", ctypes.c_size_t), ("status", _P), ("timeout_ns", ctypes.c_uint64),
+    ]
+
+
 def build() -> None:
     """Compile libcudaforge_b200.so for sm_100a (nvcc cross-compiles on CPU)."""
     subprocess.run(["make", "-s", "-j8", "-C", CSRC], check=True)
@@ -56,6 +65,11 @@ def lib() -> ctypes.CDLL:
         L.cf_accept_workspace_bytes.restype = ctypes.c_size_t
         L.cf_accept_workspace_bytes.argtypes = [_I32, _I32]
         L.cf_accept_sample.argtypes = [ctypes.POINTER(CfAcceptArgs), _P]
+        L.cf_gemm_workspace_bytes.restype = ctypes.c_size_t
+        L.cf_gemm_workspace_bytes.argtypes = [_I32, _I32, _I32, _I32, _I32]
+        for fn in ("cf_w4a16_gemm", "cf_dense_gemm"):
+            getattr(L, fn).argtypes = [ctypes.POINTER(CfGemmArgs), _P]
+        L.cf_w4a16_repack.argtypes = [_P, _P, _I32, _I32, _P]
         _lib = L
     return _lib
 

@@ -113,6 +113,55 @@ typedef struct cf_accept_args {
 size_t cf_accept_workspace_bytes(int32_t batch, int32_t k);
 int cf_accept_sample(const cf_accept_args *args, void *stream);
 
+/* ------------------------------------------------------------------------
+ * GEMM on tcgen05 tensor cores (TMEM accumulators, TMA-staged operands)
+ *
+ * cf_w4a16_gemm replaces the reference INT4 GEMM launcher
+ * launch_int4_gemm_dequant(const Int4GemmParams&, cudaStream_t)
+ * (csrc/include/cudaforge/kernels/dequantize.cuh:12-31,
+ *  csrc/kernels/cuda/int4_gemm_dequant.cu:117-133) and its tested Triton
+ * twin int4_gemm_dequant_triton (csrc/kernels/triton/int4_dequant_triton.py:80-131):
+ *     y[m, n] = sum_k x[m, k] * (nibble(k, n) - 8) * scales[k / 128, n]
+ *               (+ residual[m, n])
+ * x: bf16 [m, k] (row pitch ldx elements, 16-B aligned rows);
+ * w: packed INT4 [k/8, n] uint32 in the kernel order made by
+ *    cf_w4a16_repack from the reference packing (nibble i of word (j, n)
+ *    holds k = 8j + i; tests/unit/test_int4_dequant.py:6-15), zero point 8;
+ * scales: fp16 [k/128, n]; y: bf16 [m, n] (pitch ldy); residual optional.
+ * Requirements: n % 128 == 0, k % 128 == 0.  When the plan splits K
+ * (split_k = 0 picks it from the SM count) the fp32 partials go to
+ * `workspace` (cf_gemm_workspace_bytes) and a fixed-order reduction kernel
+ * produces y.  `status` (optional, device int) receives CF_ETIMEOUT if a
+ * bounded pipeline wait expired (timeout_ns, 0 = 2 s).
+ *
+ * cf_dense_gemm is the same kernel with 16-bit weights w [n, k] (k
+ * contiguous, nn.Linear layout) loaded by TMA instead of dequantised; act
+ * dtype CF_BF16 or CF_F16 (x, w, y, residual all of that type).
+ * ---------------------------------------------------------------------- */
+typedef struct cf_gemm_args {
+  int32_t m, n, k;
+  int32_t act_dtype;     /* cf_dtype of x / y / residual (and w when dense) */
+  const void *x;
+  int64_t ldx;
+  const void *w;
+  const void *scales;    /* int4 only */
+  void *y;
+  int64_t ldy;
+  const void *residual;  /* optional */
+  int64_t ldr;
+  int32_t split_k;       /* 0 = automatic */
+  void *workspace;
+  size_t workspace_bytes;
+  int32_t *status;       /* optional */
+  uint64_t timeout_ns;   /* 0 = default */
+} cf_gemm_args;
+
+size_t cf_gemm_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t split_k, int32_t int4);
+int cf_w4a16_gemm(const cf_gemm_args *args, void *stream);
+int cf_dense_gemm(const cf_gemm_args *args, void *stream);
+/* Reference [k/8, n] packing -> kernel nibble order (same values). */
+int cf_w4a16_repack(const uint32_t *wq_ref, uint32_t *wq_out, int32_t k, int32_t n, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,84 @@
+"""GPU: the tcgen05 W4A16 / dense GEMM against torch fp32 references.
+
+Two checks per case: (1) against the exact fp32 dequantisation
+w = (nibble - 8) * scale (the reference test's semantics,
+tests/unit/test_int4_dequant.py:18-53) with the max error relative to the
+largest output <= 1e-2; (2) against an fp32 GEMM over the bf16 weights the
+kernel actually multiplies, max relative error <= 5e-3 (bf16 output rounding) (catches any indexing
+error, which the looser bound might hide)."""
+import pytest
+import torch
+
+from cudaforge_b200.gemm import dense_gemm, dequant_reference, pack_int4_reference, repack_int4, w4a16_gemm
+
+pytestmark = pytest.mark.gpu
+
+
+def _w4(K, N, seed, scale=0.002):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randint(0, 16, (K, N), generator=g)
+    s = (torch.randn(K // 128, N, generator=g).abs() * scale).to(torch.float16)
+    return pack_int4_reference(q), s, q
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-20)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 128, 128), (64, 256, 512), (16, 256, 128), (64, 128, 512),
+                                   (384, 6144, 4096), (100, 384, 1024), (640, 256, 1024), (1000, 128, 256),
+                                   (1, 128, 128), (24, 4096, 14336)])
+@pytest.mark.parametrize("split", [0, 1])
+def test_w4a16_vs_fp32(M, N, K, split):
+    wq, s, q = _w4(K, N, M + N + K)
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    wd = dequant_reference(wq, s)
+    ref = x.float() @ wd
+    wk = repack_int4(wq.cuda())
+    y = w4a16_gemm(x.cuda(), wk, s.cuda(), split_k=split)
+    torch.cuda.synchronize()
+    assert _rel(y.cpu(), ref) < 1e-2
+    # emulate the kernel's weight rounding: bf16((q - 8) * bf16(scale))
+    sb = s.float().to(torch.bfloat16).float().repeat_interleave(128, 0)
+    w_bf = ((q.float() - 8.0) * sb).to(torch.bfloat16).float()
+    ref2 = x.float() @ w_bf
+    assert _rel(y.cpu(), ref2) < 5e-3  # bf16 output rounding is 2^-9 relative
+
+
+def test_w4a16_residual_and_strided_out():
+    M, N, K = 48, 512, 768
+    wq, s, q = _w4(K, N, 3)
+    x = torch.randn(M, K).to(torch.bfloat16)
+    r = torch.randn(M, N).to(torch.bfloat16)
+    out = torch.zeros(M, N + 64, dtype=torch.bfloat16).cuda()
+    for split in (1, 3):
+        y = w4a16_gemm(x.cuda(), repack_int4(wq.cuda()), s.cuda(), residual=r.cuda(), out=out[:, :N], split_k=split)
+        torch.cuda.synchronize()
+        ref = x.float() @ dequant_reference(wq, s) + r.float()
+        assert _rel(y.cpu(), ref) < 1e-2
+        assert (out[:, N:] == 0).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", [(32, 512, 512), (160, 1408, 512), (40, 32000, 512), (8, 128, 1408)])
+def test_dense_vs_fp32(dtype, M, N, K):
+    if N % 128:
+        pytest.skip("N must be a multiple of 128")
+    g = torch.Generator().manual_seed(M * N)
+    x = torch.randn(M, K, generator=g).to(dtype)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(dtype)
+    y = dense_gemm(x.cuda(), w.cuda())
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().T
+    assert _rel(y.cpu(), ref) < 5e-3
+
+
+def test_repack_roundtrip_values():
+    wq, s, q = _w4(256, 128, 9)
+    wk = repack_int4(wq.cuda()).cpu()
+    w = wk.to(torch.int64) & 0xFFFFFFFF
+    ks = [0, 2, 4, 6, 1, 3, 5, 7]
+    orig = wq.to(torch.int64) & 0xFFFFFFFF
+    for pos in range(8):
+        assert torch.equal((w >> (4 * pos)) & 0xF, (orig >> (4 * ks[pos])) & 0xF)
