@@ -162,6 +162,68 @@ int cf_dense_gemm(const cf_gemm_args *args, void *stream);
 /* Reference [k/8, n] packing -> kernel nibble order (same values). */
 int cf_w4a16_repack(const uint32_t *wq_ref, uint32_t *wq_out, int32_t k, int32_t n, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Paged KV cache: host page tables (reference semantics) over caller-owned
+ * device pools.
+ *
+ * Replaces cudaforge::memory::PagedKVCache
+ * (csrc/include/cudaforge/memory/paged_kv_cache.h:36-178,
+ *  csrc/src/memory/paged_kv_cache.cpp, bound in
+ *  csrc/bindings/pybind_module.cpp:27-99).  Pool layout (per pool, K and V):
+ *  [block][layer][kv_head][slot][head_dim] elements, block stride
+ *  bytes_per_block = num_layers * layer_block_bytes, layer_block_bytes =
+ *  num_kv_heads * block_size * head_dim * element_size_bytes.
+ * Errors: CF_ENOMEM where the reference throws OutOfPagesException,
+ * CF_ERANGE for an unknown sequence id (the reference's runtime_error) or a
+ * batch beyond max_supported_batch_size / max_blocks_per_sequence.
+ * ---------------------------------------------------------------------- */
+typedef struct cf_kv_config {      /* KVCacheConfig, paged_kv_cache.h:36-46 */
+  uint32_t num_layers;
+  uint32_t num_kv_heads;
+  uint32_t head_dim;
+  uint32_t block_size;
+  uint64_t element_size_bytes;
+  uint64_t total_gpu_blocks;
+  int32_t enable_prefix_caching;
+  uint64_t max_supported_batch_size;
+  uint64_t max_blocks_per_sequence;
+} cf_kv_config;
+
+typedef struct cf_kv_stats {       /* KVCacheStats, paged_kv_cache.h:63-75 */
+  uint64_t total_blocks, free_blocks, allocated_blocks, cached_prefix_blocks;
+  uint64_t total_memory_bytes, used_memory_bytes;
+  double pool_utilization_ratio;
+  uint32_t active_sequences_count;
+  uint64_t prefix_cache_hits, prefix_cache_misses, lru_evictions_count;
+} cf_kv_stats;
+
+typedef struct cf_kvcache cf_kvcache;
+
+/* PagedKVCache(config, allocator) (paged_kv_cache.cpp:9-60); NULL on bad config. */
+cf_kvcache *cf_kvcache_create(const cf_kv_config *cfg, void *key_pool, void *val_pool);
+void cf_kvcache_destroy(cf_kvcache *h);
+/* register_sequence_with_prefix (paged_kv_cache.cpp:167-253) */
+int cf_kvcache_register_sequence(cf_kvcache *h, uint64_t seq, const int32_t *tokens, uint32_t n,
+                                 uint32_t *matched_out);
+/* append_tokens (:255-286) */
+int cf_kvcache_append_tokens(cf_kvcache *h, uint64_t seq, uint32_t n);
+/* unregister_sequence (:288-299) */
+int cf_kvcache_unregister_sequence(cf_kvcache *h, uint64_t seq);
+/* fork_sequence (:301-316) */
+int cf_kvcache_fork_sequence(cf_kvcache *h, uint64_t parent, uint64_t child);
+/* get_block_table (:398-407): copies up to cap ids, *len = table length */
+int cf_kvcache_get_block_table(cf_kvcache *h, uint64_t seq, int32_t *out, uint32_t cap, uint32_t *len);
+/* prepare_batch_metadata (:318-396), host half: tables[batch][*max_blocks_out]
+ * padded with -1 (tables may be NULL to query the width), context_lens[batch].
+ * The caller copies both to the device on its stream. */
+int cf_kvcache_prepare_batch(cf_kvcache *h, const uint64_t *seqs, uint32_t batch, int32_t *tables,
+                             uint32_t table_cap, int32_t *context_lens, uint32_t *max_blocks_out);
+/* get_stats (:423-445) */
+int cf_kvcache_get_stats(cf_kvcache *h, cf_kv_stats *s);
+/* get_key_block_ptr / get_value_block_ptr (:409-421) */
+void *cf_kvcache_key_block_ptr(cf_kvcache *h, int32_t block, uint32_t layer);
+void *cf_kvcache_value_block_ptr(cf_kvcache *h, int32_t block, uint32_t layer);
+
 #ifdef __cplusplus
 }
 #endif

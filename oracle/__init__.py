@@ -136,3 +136,75 @@ def ref_verify_greedy(draft_tokens, target_probs, eos):
     ref().ref_verify_greedy(ctypes.c_int32(K), ctypes.c_int64(V), _ptr(dt), _ptr(tp),
                             ctypes.c_int32(eos), _ptr(tok), _ptr(na), _ptr(ef))
     return tok, int(na[0]), int(ef[0])
+
+
+# ---- the unmodified reference PagedKVCache (compiled with a host-memory runtime) ----
+
+class RefKV:
+    """ctypes front end to oracle/_ref/libkv_ref.so (reference PagedKVCache)."""
+
+    _L = None
+
+    @classmethod
+    def available(cls) -> bool:
+        return os.path.exists(os.path.join(HERE, "_ref", "libkv_ref.so"))
+
+    @classmethod
+    def lib(cls):
+        if cls._L is None:
+            L = ctypes.CDLL(os.path.join(HERE, "_ref", "libkv_ref.so"))
+            L.refkv_create.restype = _P
+            L.refkv_create.argtypes = [ctypes.c_uint32] * 4 + [ctypes.c_uint64, ctypes.c_int, ctypes.c_uint64,
+                                                               ctypes.c_uint64]
+            for n, a in (("refkv_destroy", [_P]), ("refkv_register", [_P, ctypes.c_uint64, _P, ctypes.c_uint32, _P]),
+                         ("refkv_append", [_P, ctypes.c_uint64, ctypes.c_uint32]),
+                         ("refkv_unregister", [_P, ctypes.c_uint64]),
+                         ("refkv_fork", [_P, ctypes.c_uint64, ctypes.c_uint64]),
+                         ("refkv_table", [_P, ctypes.c_uint64, _P, ctypes.c_uint32, _P]),
+                         ("refkv_prepare", [_P, _P, ctypes.c_uint32, _P, ctypes.c_uint32, _P, _P]),
+                         ("refkv_stats", [_P, _P])):
+                getattr(L, n).argtypes = a
+            cls._L = L
+        return cls._L
+
+    def __init__(self, layers, heads, dim, bs, total, prefix=True, max_batch=256, max_blocks=512):
+        self.h = self.lib().refkv_create(layers, heads, dim, bs, total, int(prefix), max_batch, max_blocks)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib().refkv_destroy(self.h)
+            self.h = None
+
+    def register(self, seq, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        m = ctypes.c_uint32(0)
+        rc = self.lib().refkv_register(self.h, seq, _ptr(t) if t.size else None, t.size, ctypes.byref(m))
+        return rc, m.value
+
+    def append(self, seq, n):
+        return self.lib().refkv_append(self.h, seq, n)
+
+    def unregister(self, seq):
+        return self.lib().refkv_unregister(self.h, seq)
+
+    def fork(self, p, c):
+        return self.lib().refkv_fork(self.h, p, c)
+
+    def table(self, seq):
+        buf = np.zeros(4096, np.int32)
+        n = ctypes.c_uint32(0)
+        rc = self.lib().refkv_table(self.h, seq, _ptr(buf), buf.size, ctypes.byref(n))
+        return rc, buf[: n.value].tolist()
+
+    def prepare(self, seqs):
+        ids = np.ascontiguousarray(seqs, dtype=np.uint64)
+        tab = np.zeros(len(seqs) * 4096, np.int32)
+        ctx = np.zeros(max(1, len(seqs)), np.int32)
+        mb = ctypes.c_uint32(0)
+        rc = self.lib().refkv_prepare(self.h, _ptr(ids), len(seqs), _ptr(tab), tab.size, _ptr(ctx), ctypes.byref(mb))
+        return rc, tab[: len(seqs) * mb.value].reshape(len(seqs), mb.value), ctx[: len(seqs)]
+
+    def stats(self):
+        out = np.zeros(8, np.uint64)
+        self.lib().refkv_stats(self.h, _ptr(out))
+        return out.tolist()
