@@ -44,6 +44,30 @@ class CfGemmArgs(ctypes.Structure):
     ]
 
 
+class CfKvLayout(ctypes.Structure):
+    _fields_ = [("key_pool", _P), ("val_pool", _P), ("total_blocks", _I64), ("num_layers", _I32),
+                ("num_kv_heads", _I32), ("head_dim", _I32), ("block_size", _I32), ("dtype", _I32)]
+
+
+class CfAttnArgs(ctypes.Structure):
+    _fields_ = [
+        ("kv", CfKvLayout), ("layer", _I32), ("batch", _I32), ("rows", _I32), ("num_q_heads", _I32),
+        ("q", _P), ("q_row_stride", _I64), ("k_new", _P), ("v_new", _P), ("new_kv_all_layers", _I32),
+        ("block_tables", _P), ("max_blocks", _I32), ("context_lens", _P), ("max_context", _I32),
+        ("tree_mask", _P), ("mask_words", _I32), ("out", _P), ("out_row_stride", _I64), ("scale", _F32),
+        ("num_splits", _I32), ("workspace", _P), ("workspace_bytes", ctypes.c_size_t), ("status", _P),
+        ("timeout_ns", ctypes.c_uint64),
+    ]
+
+
+class CfKvCommitArgs(ctypes.Structure):
+    _fields_ = [
+        ("kv", CfKvLayout), ("batch", _I32), ("rows", _I32), ("layer_begin", _I32), ("layer_count", _I32),
+        ("k_new", _P), ("v_new", _P), ("n_commit", _P), ("n_commit_add", _I32), ("row_index", _P),
+        ("start_pos", _P), ("block_tables", _P), ("max_blocks", _I32), ("status", _P),
+    ]
+
+
 def build() -> None:
     """Compile libcudaforge_b200.so for sm_100a (nvcc cross-compiles on CPU)."""
     subprocess.run(["make", "-s", "-j8", "-C", CSRC], check=True)
@@ -70,6 +94,14 @@ def lib() -> ctypes.CDLL:
         for fn in ("cf_w4a16_gemm", "cf_dense_gemm"):
             getattr(L, fn).argtypes = [ctypes.POINTER(CfGemmArgs), _P]
         L.cf_w4a16_repack.argtypes = [_P, _P, _I32, _I32, _P]
+        L.cf_attention_workspace_bytes.restype = ctypes.c_size_t
+        L.cf_attention_workspace_bytes.argtypes = [ctypes.POINTER(CfAttnArgs)]
+        L.cf_verify_attention.argtypes = [ctypes.POINTER(CfAttnArgs), _P]
+        L.cf_kv_commit.argtypes = [ctypes.POINTER(CfKvCommitArgs), _P]
+        L.cf_embedding.argtypes = [_P, _I32, _P, _I32, _I32, _P, _I32, _P]
+        L.cf_rmsnorm.argtypes = [_P, _I64, _P, _P, _I64, _I32, _I32, _F32, _I32, _P]
+        L.cf_rope_qkv.argtypes = [_P, _I64, _I32, _I32, _I32, _I32, _P, _F32, _P, _P, _I32, _P]
+        L.cf_silu_mul.argtypes = [_P, _I64, _P, _I64, _I32, _I32, _I32, _P]
         _lib = L
     return _lib
 

@@ -1,0 +1,478 @@
+// Paged verify attention for speculative decoding (sm_100a).
+//
+// The R new query rows of each sequence (chain: the last emitted token + K
+// drafts; tree: the root + N tree nodes) attend to
+//   * the sequence's cached context, read page by page from the paged pool
+//     [block][layer][kv_head][slot][head_dim] through TMA (two 64-column
+//     boxes with 128-B swizzle per 16-token page per tensor), and
+//   * the R new rows themselves (this step's K/V scratch), under a causal
+//     (chain) or tree-ancestor mask.
+// Semantics follow the reference's attention kernels (online softmax with
+// scale head_dim^-1/2: csrc/kernels/triton/flash_attn_triton.py:7-110,
+// csrc/kernels/cuda/flash_attn_v2.cu:46-195), extended with paging (the
+// KVCacheBatchDescriptor contract, csrc/include/cudaforge/memory/
+// paged_kv_cache.h:81-94), grouped-query heads and the tree mask.
+//
+// One CTA = (row tile of 16*NW query rows of one kv-head group) x (one KV
+// split).  Query rows of a kv head are ordered (new row r, head-in-group g).
+// Each warp owns 16 query rows; QK^T and PV use mma.sync m16n8k16 on
+// ldmatrix fragments (K non-transposed, V transposed) with fp32 online
+// softmax in registers.  The loop is HBM-bound (~24 FLOP per KV byte at
+// GQA 4:1 and 6 rows), so the legacy warp MMA is ample; the pool stream is
+// what the kernel is built around: a 4-stage TMA pipeline, 8 KB per stage.
+// Several splits per sequence (flash-decoding) are merged by
+// attn_combine_kernel in log-sum-exp form.
+#include "common.cuh"
+#include "sm100.cuh"
+#include "tmap.h"
+
+#include <algorithm>
+#include <math.h>
+
+namespace {
+
+using namespace cf::sm100;
+
+constexpr int kPage = 16;   // tokens per KV page (reference block_size 16)
+constexpr int kStages = 4;
+constexpr uint64_t kDrainNs = 1000000000ull;
+
+struct AttnParams {
+  int B, R, G, Hkv, L, layer, rows_total, nsplit, max_blocks;
+  int64_t total_blocks;
+  const void *q;
+  int64_t q_row_stride;
+  const void *k_new, *v_new;  // this layer: [B][R][Hkv][D]
+  const int32_t *block_tables, *context_lens;
+  const uint64_t *tree_mask;
+  int mask_words;
+  void *out;
+  int64_t out_row_stride;
+  float scale_log2;
+  float *ws_o, *ws_lse;
+  int *status;
+  uint64_t timeout_ns;
+};
+
+template <typename T> struct MmaOp;
+template <> struct MmaOp<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+};
+template <> struct MmaOp<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// Byte offset of 16-B chunk `c` of row `r` in a KV page tile laid out as
+// HD/64 boxes of [16 rows][128 B] with the TMA 128-B swizzle.
+template <int HD>
+__device__ __forceinline__ uint32_t kv_off(int r, int c) {
+  return (uint32_t)((c >> 3) * (kPage * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+// Q tile: rows of HD*2 bytes, chunk index XOR (row & 7).
+template <int HD>
+__device__ __forceinline__ uint32_t q_off(int r, int c) {
+  return (uint32_t)(r * (HD * 2) + ((c ^ (r & 7)) << 4));
+}
+
+template <typename T, int HD, int NW>
+__global__ void __launch_bounds__(NW * 32)
+verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                   const AttnParams p) {
+  constexpr int ROWS = 16 * NW;
+  constexpr int TILE_BYTES = kPage * HD * 2;  // one tensor, one page
+  constexpr int CH = HD / 8;                  // 16-B chunks per row
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *kv_s = smem;                                   // [kStages][K tile, V tile]
+  uint8_t *q_s = smem + kStages * 2 * TILE_BYTES;         // [ROWS][HD]
+  uint64_t *full = reinterpret_cast<uint64_t *>(q_s + ROWS * HD * 2);
+  __shared__ int s_abort;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row_tile = blockIdx.x;
+  const int b = blockIdx.y / p.Hkv, h = blockIdx.y % p.Hkv;
+  const int split = blockIdx.z;
+  const int ctx = p.context_lens[b];
+  const int pc = (ctx + kPage - 1) / kPage;       // cached pages
+  const int pn = (p.R + kPage - 1) / kPage;       // new-row tiles
+  const int T_all = pc + pn;
+  const int tps = (T_all + p.nsplit - 1) / p.nsplit;
+  const int t_begin = min(T_all, split * tps), t_end = min(T_all, t_begin + tps);
+  const int ntiles = t_end - t_begin;
+  const int32_t *btab = p.block_tables + (int64_t)b * p.max_blocks;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  // ---- Q tile -> shared (rows >= R*G are zero) ----
+  for (int idx = tid; idx < ROWS * CH; idx += NW * 32) {
+    const int r = idx / CH, c = idx % CH;
+    const int qrow = row_tile * ROWS + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (qrow < p.rows_total) {
+      const int rr = qrow / p.G, g = qrow % p.G;
+      const T *src = reinterpret_cast<const T *>(p.q) + (int64_t)(b * p.R + rr) * p.q_row_stride +
+                     (int64_t)(h * p.G + g) * HD + c * 8;
+      v = *reinterpret_cast<const uint4 *>(src);
+    }
+    *reinterpret_cast<uint4 *>(q_s + q_off<HD>(r, c)) = v;
+  }
+  __syncthreads();
+
+  // ---- producer: TMA of cached page i (of this split) into stage i % kStages ----
+  const int pool_rows_per_block = p.L * p.Hkv * kPage;
+  auto issue = [&](int i) {
+    const int t = t_begin + i;
+    if (t >= pc) return;  // new-row tiles are copied by all threads
+    const int s = i % kStages;
+    int blk = btab[t];
+    if (blk < 0 || blk >= p.total_blocks) {  // invalid page id: record and load page 0 (masked below)
+      if (p.status) atomicExch(p.status, CF_ERANGE);
+      blk = 0;
+    }
+    const int y = blk * pool_rows_per_block + (p.layer * p.Hkv + h) * kPage;
+    uint8_t *st = kv_s + s * 2 * TILE_BYTES;
+    mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
+#pragma unroll
+    for (int half = 0; half < HD / 64; ++half) {
+      tma_load_2d(st + half * kPage * 128, &tm_k, &full[s], half * 64, y);
+      tma_load_2d(st + TILE_BYTES + half * kPage * 128, &tm_v, &full[s], half * 64, y);
+    }
+  };
+  int issued = 0;
+  if (tid == 0) {
+    for (int i = 0; i < kStages - 1 && i < ntiles; ++i) { issue(i); issued = i + 1; }
+  }
+
+  // ---- per-warp state ----
+  float o[HD / 8][4];
+#pragma unroll
+  for (int d = 0; d < HD / 8; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.0f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
+  const int wrow0 = warp * 16;
+  const int qrow_a = row_tile * ROWS + wrow0 + (lane >> 2);  // rows of c0,c1 / c2,c3: +0 / +8
+  const bool warp_active = row_tile * ROWS + wrow0 < p.rows_total;
+  const uint32_t q_base = smem_u32(q_s);
+
+  for (int i = 0; i < ntiles; ++i) {
+    const int t = t_begin + i;
+    const int s = i % kStages;
+    uint8_t *st = kv_s + s * 2 * TILE_BYTES;
+    if (tid == 0 && i + kStages - 1 < ntiles) { issue(i + kStages - 1); issued = i + kStages; }
+    if (t < pc) {
+      if (!mbar_wait(&full[s], (uint32_t)(i / kStages) & 1u, p.timeout_ns)) s_abort = 1;
+    } else {
+      // new rows (t - pc)*16 .. : copy this step's K/V scratch rows into the stage
+      const int j0 = (t - pc) * kPage;
+      for (int idx = tid; idx < kPage * CH; idx += NW * 32) {
+        const int r = idx / CH, c = idx % CH;
+        const int j = j0 + r;
+        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+        if (j < p.R) {
+          const int64_t off = ((int64_t)(b * p.R + j) * p.Hkv + h) * HD + c * 8;
+          kv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.k_new) + off);
+          vv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.v_new) + off);
+        }
+        *reinterpret_cast<uint4 *>(st + kv_off<HD>(r, c)) = kv;
+        *reinterpret_cast<uint4 *>(st + TILE_BYTES + kv_off<HD>(r, c)) = vv;
+      }
+    }
+    __syncthreads();
+    if (s_abort) break;
+    if (warp_active) {
+      const uint32_t k_base = smem_u32(st), v_base = k_base + TILE_BYTES;
+      // S = Q K^T for this warp's 16 rows x 16 tokens
+      float sc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        uint32_t a[4], kb[4];
+        {
+          const int r = wrow0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int c = 2 * kk + (lane >> 4);
+          ldsm_x4(q_base + q_off<HD>(r, c), a);
+        }
+        {
+          const int tok = ((lane >> 4) << 3) + (lane & 7);
+          const int c = 2 * kk + ((lane >> 3) & 1);
+          ldsm_x4(k_base + kv_off<HD>(tok, c), kb);
+        }
+        MmaOp<T>::run(sc[0], a, kb[0], kb[1]);
+        MmaOp<T>::run(sc[1], a, kb[2], kb[3]);
+      }
+      // mask + online softmax (log2 domain)
+      float mx[2] = {m_r[0], m_r[1]};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = nt * 8 + 2 * (lane & 3) + (e & 1);
+          const int qrow = qrow_a + (e >> 1) * 8;
+          bool vis;
+          if (t < pc) {
+            vis = t * kPage + col < ctx;
+          } else {
+            const int j = (t - pc) * kPage + col;
+            const int rq = qrow / p.G;
+            if (j >= p.R || qrow >= p.rows_total) {
+              vis = false;
+            } else if (p.tree_mask) {
+              const uint64_t w = p.tree_mask[((int64_t)b * p.R + rq) * p.mask_words + (j >> 6)];
+              vis = (w >> (j & 63)) & 1ull;
+            } else {
+              vis = j <= rq;
+            }
+          }
+          const float x = vis ? sc[nt][e] * p.scale_log2 : -INFINITY;
+          sc[nt][e] = x;
+          mx[e >> 1] = fmaxf(mx[e >> 1], x);
+        }
+      }
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
+        mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
+      }
+      float corr[2];
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        corr[hr] = (m_r[hr] == -INFINITY) ? 0.0f : exp2f(m_r[hr] - mx[hr]);
+        if (mx[hr] == -INFINITY) corr[hr] = 1.0f;
+        m_r[hr] = mx[hr];
+        l_r[hr] *= corr[hr];
+      }
+      uint32_t pa[4];
+      {
+        float pv[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float mm = m_r[e >> 1];
+            const float pe = (mm == -INFINITY) ? 0.0f : exp2f(sc[nt][e] - mm);
+            pv[nt][e] = pe;
+            l_r[e >> 1] += pe;
+          }
+        pa[0] = MmaOp<T>::pack(pv[0][0], pv[0][1]);
+        pa[1] = MmaOp<T>::pack(pv[0][2], pv[0][3]);
+        pa[2] = MmaOp<T>::pack(pv[1][0], pv[1][1]);
+        pa[3] = MmaOp<T>::pack(pv[1][2], pv[1][3]);
+      }
+#pragma unroll
+      for (int d = 0; d < HD / 8; ++d) {
+        o[d][0] *= corr[0]; o[d][1] *= corr[0];
+        o[d][2] *= corr[1]; o[d][3] *= corr[1];
+      }
+      // O += P V
+#pragma unroll
+      for (int dp = 0; dp < HD / 16; ++dp) {
+        uint32_t vb[4];
+        const int tok = (((lane >> 3) & 1) << 3) + (lane & 7);
+        const int c = 2 * dp + (lane >> 4);
+        ldsm_x4_t(v_base + kv_off<HD>(tok, c), vb);
+        MmaOp<T>::run(o[2 * dp], pa, vb[0], vb[1]);
+        MmaOp<T>::run(o[2 * dp + 1], pa, vb[2], vb[3]);
+      }
+    }
+    __syncthreads();  // stage s is free for the prefetch issued next iteration
+  }
+
+  if (s_abort) {
+    if (p.status) atomicExch(p.status, CF_ETIMEOUT);
+    if (tid == 0)  // let our own copies land before the CTA exits
+      for (int j = max(0, issued - kStages); j < issued; ++j)
+        if (t_begin + j < pc) mbar_wait(&full[j % kStages], (uint32_t)(j / kStages) & 1u, kDrainNs);
+    return;
+  }
+  if (!warp_active) return;
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 1);
+    l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 2);
+  }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int qrow = qrow_a + hr * 8;
+    if (qrow >= p.rows_total) continue;
+    const int rr = qrow / p.G, g = qrow % p.G;
+    const float inv = l_r[hr] > 0.0f ? 1.0f / l_r[hr] : 0.0f;
+    if (p.nsplit == 1) {
+      T *dst = reinterpret_cast<T *>(p.out) + (int64_t)(b * p.R + rr) * p.out_row_stride + (int64_t)(h * p.G + g) * HD;
+#pragma unroll
+      for (int d = 0; d < HD / 8; ++d) {
+        const int col = d * 8 + 2 * (lane & 3);
+        *reinterpret_cast<uint32_t *>(dst + col) = MmaOp<T>::pack(o[d][2 * hr] * inv, o[d][2 * hr + 1] * inv);
+      }
+    } else {
+      const int64_t rowid = (((int64_t)split * p.B + b) * p.Hkv + h) * p.rows_total + qrow;
+      float *dst = p.ws_o + rowid * HD;
+#pragma unroll
+      for (int d = 0; d < HD / 8; ++d) {
+        const int col = d * 8 + 2 * (lane & 3);
+        *reinterpret_cast<float2 *>(dst + col) = make_float2(o[d][2 * hr] * inv, o[d][2 * hr + 1] * inv);
+      }
+      if ((lane & 3) == 0) p.ws_lse[rowid] = (l_r[hr] > 0.0f) ? m_r[hr] + log2f(l_r[hr]) : -INFINITY;
+    }
+  }
+}
+
+// Merge the per-split partial outputs (normalised O_s, lse_s in log2 units).
+template <typename T, int HD>
+__global__ void attn_combine_kernel(const AttnParams p) {
+  const int bh = blockIdx.x, qrow = blockIdx.y;
+  const int b = bh / p.Hkv, h = bh % p.Hkv;
+  const int64_t stride = (int64_t)p.B * p.Hkv * p.rows_total;
+  const int64_t base = ((int64_t)b * p.Hkv + h) * p.rows_total + qrow;
+  float mx = -INFINITY;
+  for (int s = 0; s < p.nsplit; ++s) mx = fmaxf(mx, p.ws_lse[s * stride + base]);
+  const int rr = qrow / p.G, g = qrow % p.G;
+  T *dst = reinterpret_cast<T *>(p.out) + (int64_t)(b * p.R + rr) * p.out_row_stride + (int64_t)(h * p.G + g) * HD;
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float num = 0.0f, den = 0.0f;
+    for (int s = 0; s < p.nsplit; ++s) {
+      const float l = p.ws_lse[s * stride + base];
+      if (l == -INFINITY) continue;
+      const float w = exp2f(l - mx);
+      num += w * p.ws_o[(s * stride + base) * HD + d];
+      den += w;
+    }
+    const float v = den > 0.0f ? num / den : 0.0f;
+    if constexpr (std::is_same<T, __half>::value) dst[d] = __float2half_rn(v);
+    else dst[d] = __float2bfloat16_rn(v);
+  }
+}
+
+int pick_splits(const cf_attn_args &a, int row_tiles) {
+  if (a.num_splits > 0) return a.num_splits;
+  int sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int ctas = a.batch * a.kv.num_kv_heads * row_tiles;
+  const int want = (4 * sms + ctas - 1) / ctas;
+  const int pages = (a.max_context + kPage - 1) / kPage;
+  return std::max(1, std::min(want, std::max(1, pages / 8)));
+}
+
+template <typename T, int HD, int NW>
+int launch(const cf_attn_args &a, cudaStream_t stream) {
+  constexpr int ROWS = 16 * NW;
+  const int G = a.num_q_heads / a.kv.num_kv_heads;
+  AttnParams p;
+  p.B = a.batch; p.R = a.rows; p.G = G; p.Hkv = a.kv.num_kv_heads; p.L = a.kv.num_layers; p.layer = a.layer;
+  p.rows_total = a.rows * G;
+  const int row_tiles = (p.rows_total + ROWS - 1) / ROWS;
+  p.nsplit = pick_splits(a, row_tiles);
+  p.max_blocks = a.max_blocks; p.total_blocks = a.kv.total_blocks;
+  p.q = a.q; p.q_row_stride = a.q_row_stride;
+  const int64_t layer_new = (int64_t)a.batch * a.rows * p.Hkv * HD;
+  p.k_new = reinterpret_cast<const T *>(a.k_new) + (a.new_kv_all_layers ? layer_new * a.layer : 0);
+  p.v_new = reinterpret_cast<const T *>(a.v_new) + (a.new_kv_all_layers ? layer_new * a.layer : 0);
+  p.block_tables = a.block_tables; p.context_lens = a.context_lens;
+  p.tree_mask = a.tree_mask; p.mask_words = a.mask_words;
+  p.out = a.out; p.out_row_stride = a.out_row_stride;
+  const float scale = a.scale > 0.0f ? a.scale : 1.0f / sqrtf((float)HD);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = a.status;
+  p.timeout_ns = a.timeout_ns ? a.timeout_ns : 2000000000ull;
+  if (p.nsplit > 1) {
+    const size_t rows = (size_t)p.nsplit * p.B * p.Hkv * p.rows_total;
+    const size_t need = rows * HD * sizeof(float) + rows * sizeof(float);
+    if (!a.workspace || a.workspace_bytes < need || (reinterpret_cast<uintptr_t>(a.workspace) & 15)) return CF_EINVAL;
+    p.ws_o = reinterpret_cast<float *>(a.workspace);
+    p.ws_lse = p.ws_o + rows * HD;
+  } else {
+    p.ws_o = p.ws_lse = nullptr;
+  }
+  const CUtensorMapDataType tdt =
+      std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t pool_rows = (uint64_t)a.kv.total_blocks * p.L * p.Hkv * kPage;
+  if (pool_rows > (uint64_t)INT32_MAX) return CF_EUNSUPPORTED;
+  CUtensorMap tk, tv;
+  if (!cf::make_tmap_2d(&tk, tdt, a.kv.key_pool, HD, pool_rows, HD * 2, 64, kPage, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !cf::make_tmap_2d(&tv, tdt, a.kv.val_pool, HD, pool_rows, HD * 2, 64, kPage, CU_TENSOR_MAP_SWIZZLE_128B))
+    return CF_EINVAL;
+  const size_t smem = 1024 + kStages * 2 * kPage * HD * 2 + ROWS * HD * 2 + kStages * 8;
+  auto kern = verify_attn_kernel<T, HD, NW>;
+  CF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid(row_tiles, p.B * p.Hkv, p.nsplit);
+  kern<<<grid, NW * 32, smem, stream>>>(tk, tv, p);
+  if (cudaGetLastError() != cudaSuccess) return CF_ECUDA;
+  if (p.nsplit > 1) {
+    dim3 g2(p.B * p.Hkv, p.rows_total);
+    attn_combine_kernel<T, HD><<<g2, HD / 2 >= 32 ? HD / 2 : 32, 0, stream>>>(p);
+  }
+  return cf_launch_status();
+}
+
+template <typename T>
+int dispatch(const cf_attn_args &a, cudaStream_t s) {
+  const int G = a.num_q_heads / a.kv.num_kv_heads;
+  const bool small = a.rows * G <= 32;
+  if (a.kv.head_dim == 128) return small ? launch<T, 128, 2>(a, s) : launch<T, 128, 4>(a, s);
+  if (a.kv.head_dim == 64) return small ? launch<T, 64, 2>(a, s) : launch<T, 64, 4>(a, s);
+  return CF_EUNSUPPORTED;
+}
+
+}  // namespace
+
+extern "C" size_t cf_attention_workspace_bytes(const cf_attn_args *a) {
+  if (!a || a->kv.num_kv_heads <= 0 || a->num_q_heads % a->kv.num_kv_heads) return 0;
+  const int G = a->num_q_heads / a->kv.num_kv_heads;
+  const int rows_total = a->rows * G;
+  const int ROWS = rows_total <= 32 ? 32 : 64;
+  const int nsplit = pick_splits(*a, (rows_total + ROWS - 1) / ROWS);
+  if (nsplit <= 1) return 0;
+  const size_t rows = (size_t)nsplit * a->batch * a->kv.num_kv_heads * rows_total;
+  return rows * a->kv.head_dim * sizeof(float) + rows * sizeof(float);
+}
+
+extern "C" int cf_verify_attention(const cf_attn_args *args, void *stream) {
+  if (!args) return CF_EINVAL;
+  const cf_attn_args &a = *args;
+  if (a.batch < 0 || a.rows <= 0 || a.kv.num_kv_heads <= 0 || a.num_q_heads % a.kv.num_kv_heads) return CF_EINVAL;
+  if (a.batch == 0) return CF_OK;
+  if (a.kv.block_size != kPage || a.layer < 0 || a.layer >= a.kv.num_layers) return CF_EINVAL;
+  if (!a.q || !a.k_new || !a.v_new || !a.block_tables || !a.context_lens || !a.out) return CF_EINVAL;
+  if (!a.kv.key_pool || !a.kv.val_pool || a.kv.total_blocks <= 0) return CF_EINVAL;
+  if (a.tree_mask && a.mask_words * 64 < a.rows) return CF_EINVAL;
+  if ((a.q_row_stride % 8) || (a.out_row_stride % 8) || (reinterpret_cast<uintptr_t>(a.q) & 15) ||
+      (reinterpret_cast<uintptr_t>(a.k_new) & 15) || (reinterpret_cast<uintptr_t>(a.v_new) & 15))
+    return CF_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (a.kv.dtype == CF_BF16) return dispatch<__nv_bfloat16>(a, s);
+  if (a.kv.dtype == CF_F16) return dispatch<__half>(a, s);
+  return CF_EUNSUPPORTED;
+}

@@ -224,6 +224,121 @@ int cf_kvcache_get_stats(cf_kvcache *h, cf_kv_stats *s);
 void *cf_kvcache_key_block_ptr(cf_kvcache *h, int32_t block, uint32_t layer);
 void *cf_kvcache_value_block_ptr(cf_kvcache *h, int32_t block, uint32_t layer);
 
+/* ------------------------------------------------------------------------
+ * Device view of the paged KV pools (the KVCacheBatchDescriptor contract,
+ * csrc/include/cudaforge/memory/paged_kv_cache.h:81-94).
+ * ---------------------------------------------------------------------- */
+typedef struct cf_kv_layout {
+  void *key_pool;        /* [total_blocks][num_layers][num_kv_heads][block_size][head_dim] */
+  void *val_pool;
+  int64_t total_blocks;
+  int32_t num_layers, num_kv_heads, head_dim, block_size;
+  int32_t dtype;         /* CF_BF16 or CF_F16 */
+} cf_kv_layout;
+
+/* ------------------------------------------------------------------------
+ * Paged verify attention over the cached context plus R new rows.
+ *
+ * Replaces the reference attention launchers launch_flash_attn_v2
+ * (csrc/include/cudaforge/kernels/flash_attn_v2.h:12-31,
+ *  csrc/kernels/cuda/flash_attn_v2.cu:197-221) and flash_attn_triton
+ * (csrc/kernels/triton/flash_attn_triton.py:112-172), which take contiguous
+ * [B, H, S, D] tensors and a causal flag; this one reads the paged pool
+ * through block tables, handles grouped-query heads and a tree mask.
+ * q: row (b*R + r), head hq at q + (b*R + r)*q_row_stride + hq*head_dim;
+ * k_new / v_new: this step's new rows [B][R][Hkv][D] for `layer` (or
+ *   [L][B][R][Hkv][D] when new_kv_all_layers != 0);
+ * block_tables [B][max_blocks] (-1 padded), context_lens [B] = cached tokens
+ *   (the new rows follow them); max_context = max over context_lens (host);
+ * tree_mask NULL: causal chain (new row r sees new rows j <= r); else
+ *   [B][R][mask_words] uint64 bits, bit j of row r = r may see new row j;
+ * out: same addressing as q (out_row_stride); scale 0 = head_dim^-1/2.
+ * head_dim 64 or 128, block_size 16.  Split-KV partials use `workspace`
+ * (cf_attention_workspace_bytes); num_splits 0 = automatic.
+ * A block id outside [0, total_blocks) sets *status = CF_ERANGE and that page
+ * reads block 0; an expired pipeline wait sets CF_ETIMEOUT.
+ * ---------------------------------------------------------------------- */
+typedef struct cf_attn_args {
+  cf_kv_layout kv;
+  int32_t layer;
+  int32_t batch, rows, num_q_heads;
+  const void *q;
+  int64_t q_row_stride;
+  const void *k_new, *v_new;
+  int32_t new_kv_all_layers;
+  const int32_t *block_tables;
+  int32_t max_blocks;
+  const int32_t *context_lens;
+  int32_t max_context;
+  const uint64_t *tree_mask;
+  int32_t mask_words;
+  void *out;
+  int64_t out_row_stride;
+  float scale;
+  int32_t num_splits;
+  void *workspace;
+  size_t workspace_bytes;
+  int32_t *status;
+  uint64_t timeout_ns;
+} cf_attn_args;
+
+size_t cf_attention_workspace_bytes(const cf_attn_args *args);
+int cf_verify_attention(const cf_attn_args *args, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Accepted-KV commit: copy the surviving new rows of every layer from the
+ * step's scratch into their paged slots.
+ *
+ * The reference never writes KV (its engine only advances page tables,
+ * cudaforge/engine.py:222-224 -> PagedKVCache::append_tokens,
+ * paged_kv_cache.cpp:255-286); this is the device half of that commit.
+ * For sequence b, committed token j < n_b (n_b = n_commit[b] + n_commit_add)
+ * comes from scratch row row_index[b][j] (identity when NULL; tree paths pass
+ * the accepted node rows) and lands at position start_pos[b] + j, i.e. slot
+ * (pos % block_size) of block block_tables[b][pos / block_size], for every
+ * layer in [layer_begin, layer_begin + layer_count) and every kv head.
+ * k_new / v_new: [L][B][R][Hkv][D].  Invalid destinations set *status =
+ * CF_ERANGE and are skipped.
+ * ---------------------------------------------------------------------- */
+typedef struct cf_kv_commit_args {
+  cf_kv_layout kv;
+  int32_t batch, rows;
+  int32_t layer_begin, layer_count;
+  const void *k_new, *v_new;
+  const int32_t *n_commit;
+  int32_t n_commit_add;
+  const int32_t *row_index;
+  const int32_t *start_pos;
+  const int32_t *block_tables;
+  int32_t max_blocks;
+  int32_t *status;
+} cf_kv_commit_args;
+
+int cf_kv_commit(const cf_kv_commit_args *args, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Fused elementwise pieces of the verify forward (bf16 or fp16 `dtype`).
+ * ---------------------------------------------------------------------- */
+/* out[m, :] = table[ids[m], :]  (ids outside [0, vocab) give zero rows) */
+int cf_embedding(const int32_t *ids, int32_t m, const void *table, int32_t vocab, int32_t dim, void *out,
+                 int32_t dtype, void *stream);
+/* RMSNorm: out = x * rsqrt(mean(x^2) + eps) * w, fp32 math
+ * (csrc/kernels/cuda/fused_rmsnorm.cu:53-144 without the residual add, which
+ * the producing GEMM epilogue fuses). Rows of `dim` elements, pitches in
+ * elements. */
+int cf_rmsnorm(const void *x, int64_t ldx, const void *w, void *out, int64_t ldo, int32_t m, int32_t dim,
+               float eps, int32_t dtype, void *stream);
+/* Half-split RoPE (csrc/include/cudaforge/kernels/rope.cuh:13-31:
+ * o1 = x1 c - x2 s, o2 = x1 s + x2 c; angle = pos * base^(-2i/D)) on the
+ * fused QKV rows qkv[m][(Hq + 2 Hkv) * D] (m = b*R + r, position pos[m]):
+ * q is rotated in place; rotated k and plain v go to k_new / v_new
+ * [B][R][Hkv][D] (this layer's slice). */
+int cf_rope_qkv(void *qkv, int64_t ld, int32_t m, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                const int32_t *pos, float base, void *k_new, void *v_new, int32_t dtype, void *stream);
+/* SwiGLU: out[m, j] = silu(gu[m, j]) * gu[m, ffn + j] */
+int cf_silu_mul(const void *gu, int64_t ldg, void *out, int64_t ldo, int32_t m, int32_t ffn, int32_t dtype,
+                void *stream);
+
 #ifdef __cplusplus
 }
 #endif
