@@ -334,7 +334,7 @@ int run_gemm(const cf_gemm_args &a, cudaStream_t stream) {
   const bool int4 = WM == kInt4;
   if (a.m < 0 || a.n <= 0 || a.k <= 0) return CF_EINVAL;
   if (a.m == 0) return CF_OK;
-  if (a.n % BN != 0 || a.k % 128 != 0) return CF_EINVAL;
+  if (a.n % BN != 0 || a.k % (int4 ? 128 : BK) != 0) return CF_EINVAL;
   if (!a.x || !a.w || !a.y || (int4 && !a.scales)) return CF_EINVAL;
   if (a.ldx < a.k || a.ldy < a.n || (a.residual && a.ldr < a.n)) return CF_EINVAL;
   Plan pl;

@@ -1,0 +1,184 @@
+"""Llama-shaped target / draft models for the verify forward (random init).
+
+The reference has no model (ModelRunner::step emits `last + 1`,
+csrc/src/engine/model_runner.cpp:106-173); its speculative engine takes any
+runner with `.forward(input_ids, kv_cache_handles) -> logits[B, S, V]`
+(cudaforge/speculative.py:30-55).  This module provides that runner, built
+from this library's kernels only: per layer RMSNorm -> QKV (W4A16 or dense) ->
+RoPE + K/V scatter -> paged verify attention -> O-proj (+residual, fused in
+the GEMM epilogue) -> RMSNorm -> gate|up -> SwiGLU -> down (+residual); final
+RMSNorm -> lm_head.  Only the R new rows of each sequence are computed; the
+cached context is read from the paged pool.
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import List, Optional
+
+import torch
+
+from . import ops
+from .gemm import dense_gemm, w4a16_gemm
+
+
+@dataclasses.dataclass(frozen=True)
+class LlamaConfig:
+    layers: int
+    d_model: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    rope_base: float = 10000.0
+    eps: float = 1e-6
+    quant: str = "int4"          # "int4" (W4A16, group 128) or "dense"
+    dtype: torch.dtype = torch.bfloat16
+
+    @property
+    def qkv_dim(self):
+        return (self.n_heads + 2 * self.n_kv_heads) * self.head_dim
+
+    def linear_shapes(self):
+        """(name, N, K) of every per-layer projection plus the lm_head."""
+        d = self.d_model
+        return [("qkv", self.qkv_dim, d), ("o", d, self.n_heads * self.head_dim), ("gate_up", 2 * self.ffn, d),
+                ("down", d, self.ffn)]
+
+    def gemm_flops(self, tokens: int) -> float:
+        per_layer = sum(2.0 * n * k for _, n, k in self.linear_shapes())
+        return tokens * (self.layers * per_layer + 2.0 * self.vocab * self.d_model)
+
+    def weight_bytes(self) -> float:
+        """Bytes of the GEMM weights as stored (INT4 + fp16 group scales, or 16-bit dense)."""
+        params = self.layers * sum(n * k for _, n, k in self.linear_shapes()) + self.vocab * self.d_model
+        return params * (0.5 + 2.0 / 128) if self.quant == "int4" else params * 2.0
+
+
+# BASELINE configurations
+TINY_TARGET = LlamaConfig(4, 512, 8, 8, 64, 1408, 32000, quant="dense", dtype=torch.float16)
+TINY_DRAFT = LlamaConfig(1, 256, 4, 4, 64, 704, 32000, quant="dense", dtype=torch.float16)
+LLAMA_8B = LlamaConfig(32, 4096, 32, 8, 128, 14336, 128256)
+DRAFT_1B = LlamaConfig(16, 2048, 32, 8, 64, 8192, 128256)
+LLAMA_70B = LlamaConfig(80, 8192, 64, 8, 128, 28672, 128256)
+
+
+class Linear:
+    """One projection y = x W^T: INT4 (kernel-packed [K/8, N] + fp16 scales
+    [K/128, N]) or dense 16-bit [N, K]."""
+
+    def __init__(self, n: int, k: int, cfg: LlamaConfig, gen: torch.Generator, device, std=0.02,
+                 int4_scale=0.002):
+        self.n, self.k, self.quant = n, k, cfg.quant
+        if cfg.quant == "int4":
+            # every nibble uniform in 0..15 (value = nibble - 8 in [-8, 7]); uniform random
+            # words are uniform in any nibble order, so they serve directly as kernel-packed weights
+            self.wq = torch.randint(-2**31, 2**31 - 1, (k // 8, n), generator=gen, device=device, dtype=torch.int32)
+            self.scales = (torch.randn(k // 128, n, generator=gen, device=device).abs() * int4_scale).to(torch.float16)
+        else:
+            self.w = (torch.randn(n, k, generator=gen, device=device) * std).to(cfg.dtype)
+
+    def __call__(self, x, out=None, residual=None, workspace=None):
+        if self.quant == "int4":
+            return w4a16_gemm(x, self.wq, self.scales, out=out, residual=residual, workspace=workspace)
+        return dense_gemm(x, self.w, out=out, residual=residual, workspace=workspace)
+
+
+class LlamaModel:
+    """Random-init Llama-shaped model (seeded), resident on one device."""
+
+    def __init__(self, cfg: LlamaConfig, device="cuda", seed: int = 0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        dt = cfg.dtype
+        self.embed = (torch.randn(cfg.vocab, cfg.d_model, generator=g, device=self.device) * 0.02).to(dt)
+        self.layers = []
+        for _ in range(cfg.layers):
+            lay = {
+                "attn_norm": (torch.randn(cfg.d_model, generator=g, device=self.device) * 0.02 + 1.0).to(dt),
+                "ffn_norm": (torch.randn(cfg.d_model, generator=g, device=self.device) * 0.02 + 1.0).to(dt),
+            }
+            for name, n, k in cfg.linear_shapes():
+                lay[name] = Linear(n, k, cfg, g, self.device)
+            self.layers.append(lay)
+        self.final_norm = (torch.randn(cfg.d_model, generator=g, device=self.device) * 0.02 + 1.0).to(dt)
+        self.lm_head = Linear(cfg.vocab, cfg.d_model, cfg, g, self.device)
+        self._bufs = {}
+
+    # ---- scratch buffers, sized once per (B, R) and reused (graph friendly) ----
+    def buffers(self, B: int, R: int):
+        key = (B, R)
+        if key not in self._bufs:
+            c, M, dev, dt = self.cfg, B * R, self.device, self.cfg.dtype
+            self._bufs[key] = {
+                "h": torch.empty(M, c.d_model, dtype=dt, device=dev),
+                "xn": torch.empty(M, c.d_model, dtype=dt, device=dev),
+                "qkv": torch.empty(M, c.qkv_dim, dtype=dt, device=dev),
+                "attn": torch.empty(M, c.n_heads * c.head_dim, dtype=dt, device=dev),
+                "gu": torch.empty(M, 2 * c.ffn, dtype=dt, device=dev),
+                "act": torch.empty(M, c.ffn, dtype=dt, device=dev),
+                "logits": torch.empty(M, c.vocab, dtype=dt, device=dev),
+                "k_new": torch.empty(c.layers, B, R, c.n_kv_heads, c.head_dim, dtype=dt, device=dev),
+                "v_new": torch.empty(c.layers, B, R, c.n_kv_heads, c.head_dim, dtype=dt, device=dev),
+            }
+        return self._bufs[key]
+
+    def forward_rows(self, cache, tokens: torch.Tensor, positions: torch.Tensor, block_tables: torch.Tensor,
+                     context_lens: torch.Tensor, max_context: int, tree_mask: Optional[torch.Tensor] = None,
+                     status: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """tokens [B, R] int32 (row 0 = last emitted token, then drafts / tree
+        nodes), positions [B*R] int32, block tables / context lengths from the
+        cache (context = tokens already in the pool).  Returns logits [B*R, V]
+        (a reused buffer) and leaves this step's K/V rows in buffers()["k_new"/"v_new"]."""
+        c = self.cfg
+        B, R = tokens.shape
+        bf = self.buffers(B, R)
+        h, xn, qkv, attn, gu, act = bf["h"], bf["xn"], bf["qkv"], bf["attn"], bf["gu"], bf["act"]
+        ops.embedding(tokens.reshape(-1), self.embed, out=h)
+        for li, lay in enumerate(self.layers):
+            ops.rmsnorm(h, lay["attn_norm"], c.eps, out=xn)
+            lay["qkv"](xn, out=qkv)
+            ops.rope_qkv(qkv, positions, c.n_heads, c.n_kv_heads, c.head_dim, bf["k_new"][li], bf["v_new"][li],
+                         base=c.rope_base)
+            ops.verify_attention(cache, li, qkv, bf["k_new"][li], bf["v_new"][li], block_tables, context_lens,
+                                 max_context, rows=R, num_q_heads=c.n_heads, out=attn, tree_mask=tree_mask,
+                                 status=status)
+            lay["o"](attn, out=h, residual=h)
+            ops.rmsnorm(h, lay["ffn_norm"], c.eps, out=xn)
+            lay["gate_up"](xn, out=gu)
+            ops.silu_mul(gu, c.ffn, out=act)
+            lay["down"](act, out=h, residual=h)
+        ops.rmsnorm(h, self.final_norm, c.eps, out=xn)
+        self.lm_head(xn, out=bf["logits"])
+        return bf["logits"]
+
+    def make_cache(self, total_blocks: int, max_batch: int = 256, max_blocks_per_seq: int = 512,
+                   prefix_caching: bool = False):
+        from .kv_cache import KVCacheConfig, PagedKVCache
+        c = self.cfg
+        kc = KVCacheConfig(num_layers=c.layers, num_kv_heads=c.n_kv_heads, head_dim=c.head_dim, block_size=16,
+                           element_size_bytes=2, total_gpu_blocks=total_blocks,
+                           enable_prefix_caching=prefix_caching, max_supported_batch_size=max_batch,
+                           max_blocks_per_sequence=max_blocks_per_seq)
+        return PagedKVCache(kc, dtype=c.dtype)
+
+
+def dequant_int4_kernel_packed(wq: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """fp32 [K, N] weights of a kernel-packed INT4 Linear (for the fp32 oracle):
+    kernel nibble position p holds k = 2p (p < 4) or 2(p-4)+1 (p >= 4)."""
+    Kp, N = wq.shape
+    w = wq.to(torch.int64) & 0xFFFFFFFF
+    order = [0, 2, 4, 6, 1, 3, 5, 7]
+    q = torch.empty(Kp, 8, N, dtype=torch.float32, device=wq.device)
+    for pos in range(8):
+        q[:, order[pos], :] = ((w >> (4 * pos)) & 0xF).float()
+    q = q.reshape(Kp * 8, N)
+    return (q - 8.0) * scales.float().repeat_interleave(128, dim=0)
+
+
+def linear_weight_fp32(lin: Linear) -> torch.Tensor:
+    """[N, K] fp32 view of a projection's weights (exact dequantisation)."""
+    if lin.quant == "int4":
+        return dequant_int4_kernel_packed(lin.wq, lin.scales).T.contiguous()
+    return lin.w.float()

@@ -128,7 +128,7 @@ int cf_accept_sample(const cf_accept_args *args, void *stream);
  *    cf_w4a16_repack from the reference packing (nibble i of word (j, n)
  *    holds k = 8j + i; tests/unit/test_int4_dequant.py:6-15), zero point 8;
  * scales: fp16 [k/128, n]; y: bf16 [m, n] (pitch ldy); residual optional.
- * Requirements: n % 128 == 0, k % 128 == 0.  When the plan splits K
+ * Requirements: n % 128 == 0, k % 128 == 0 (k % 64 == 0 for cf_dense_gemm).  When the plan splits K
  * (split_k = 0 picks it from the SM count) the fp32 partials go to
  * `workspace` (cf_gemm_workspace_bytes) and a fixed-order reduction kernel
  * produces y.  `status` (optional, device int) receives CF_ETIMEOUT if a

@@ -70,3 +70,42 @@ def verify_attention(q, k_pool, v_pool, layer, tables, ctx_lens, k_new, v_new, t
         p = torch.softmax(s, dim=-1)
         out[b] = torch.einsum("hrt,thd->rhd", p, vv)
     return out
+
+
+def forward_full(model, tokens, tree_parent=None):
+    """fp32 forward of a whole sequence batch tokens [B, S] (positions 0..S-1,
+    causal) through the random-init model `model` (cudaforge_b200.model.
+    LlamaModel), using exactly dequantised weights.  Returns logits [B, S, V]
+    fp32.  This recomputes everything from the token ids; it shares no state
+    with the paged cache."""
+    from cudaforge_b200.model import linear_weight_fp32
+
+    c = model.cfg
+    B, S = tokens.shape
+    dev = model.embed.device
+    x = model.embed.float()[tokens.long().to(dev)]  # [B, S, d]
+    pos = torch.arange(S, device=dev).view(1, S, 1)
+    causal = torch.tril(torch.ones(S, S, dtype=torch.bool, device=dev))
+    G = c.n_heads // c.n_kv_heads
+    for lay in model.layers:
+        xn = rmsnorm(x, lay["attn_norm"], c.eps)
+        qkv = xn @ linear_weight_fp32(lay["qkv"]).T
+        # the kernels round activations to the model dtype between ops; mirror that at op boundaries
+        q = qkv[..., : c.n_heads * c.head_dim].view(B, S, c.n_heads, c.head_dim)
+        k = qkv[..., c.n_heads * c.head_dim:(c.n_heads + c.n_kv_heads) * c.head_dim].view(B, S, c.n_kv_heads,
+                                                                                           c.head_dim)
+        v = qkv[..., (c.n_heads + c.n_kv_heads) * c.head_dim:].view(B, S, c.n_kv_heads, c.head_dim)
+        q = rope(q, pos, c.rope_base)
+        k = rope(k, pos, c.rope_base)
+        kk = k.repeat_interleave(G, dim=2)
+        vv = v.repeat_interleave(G, dim=2)
+        s = torch.einsum("bqhd,bkhd->bhqk", q, kk) / math.sqrt(c.head_dim)
+        s = s.masked_fill(~causal, float("-inf"))
+        a = torch.einsum("bhqk,bkhd->bqhd", torch.softmax(s, -1), vv).reshape(B, S, -1)
+        x = x + a @ linear_weight_fp32(lay["o"]).T
+        xn = rmsnorm(x, lay["ffn_norm"], c.eps)
+        gu = xn @ linear_weight_fp32(lay["gate_up"]).T
+        act = torch.nn.functional.silu(gu[..., : c.ffn]) * gu[..., c.ffn:]
+        x = x + act @ linear_weight_fp32(lay["down"]).T
+    x = rmsnorm(x, model.final_norm, c.eps)
+    return x @ linear_weight_fp32(model.lm_head).T
