@@ -1,0 +1,541 @@
+#!/usr/bin/env python
+"""Benchmark: accepted tokens/s of the speculative verify + accept step on
+the Llama-3-8B-shaped W4A16 target (batch 64 per GPU,
+random 1024-token prompts, K=5 chain drafts from the 1B-shaped INT4 draft,
+T=1.0, paged KV block 16).
+
+A step = target verify forward over K+1 rows per sequence + fused acceptance
++ page-table commit and K/V commit (cudaforge_b200.BatchVerifier.step).  The
+draft model runs once before timing (its cost is excluded from the metric);
+every step uses fresh uniforms.  Requests are batch-sharded: each rank owns
+64 sequences with its own weights, pools and page tables and no collective
+(weak scaling).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "accepted tok/s of verify+accept at 8B-INT4"
+UNIT = "tokens/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.idx = gpu_index
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- timing helpers
+class KernelTimer:
+    """CUDA events around launch groups on the launching (current) stream."""
+
+    def __init__(self):
+        self.ev = {}
+
+    def __call__(self, kind):
+        timer = self
+
+        class _C:
+            def __enter__(self_):
+                self_.a = torch.cuda.Event(enable_timing=True)
+                self_.a.record()
+                return self_
+
+            def __exit__(self_, *exc):
+                b = torch.cuda.Event(enable_timing=True)
+                b.record()
+                timer.ev.setdefault(kind, []).append((self_.a, b))
+                return False
+
+        return _C()
+
+    def total_ms(self, kind):
+        return sum(a.elapsed_time(b) for a, b in self.ev.get(kind, []))
+
+    def count(self, kind):
+        return len(self.ev.get(kind, []))
+
+
+def setup(args, rank, device):
+    from cudaforge_b200.model import DRAFT_1B, LLAMA_8B, TINY_DRAFT, TINY_TARGET, LlamaModel
+    from cudaforge_b200.runner import PagedRunner
+    from cudaforge_b200.speculative import SpeculativeEngine
+    from cudaforge_b200.verifier import BatchVerifier
+
+    tcfg, dcfg = (LLAMA_8B, DRAFT_1B) if args.config == "8b" else (TINY_TARGET, TINY_DRAFT)
+    B, P, K = args.batch, args.ctx, args.k
+    steps_total = args.warmup + 2 * args.steps + 4
+    blocks_per_seq = math.ceil((P + steps_total * (K + 1)) / 16) + 2
+    target = LlamaModel(tcfg, device=device, seed=1000 + rank)
+    cache = target.make_cache(B * blocks_per_seq + 8, max_batch=B, max_blocks_per_seq=blocks_per_seq + 4)
+    ver = BatchVerifier(target, cache, list(range(B)), K, temperature=args.temperature,
+                        max_blocks_per_seq=blocks_per_seq + 4)
+    g = torch.Generator().manual_seed(7 + rank)
+    prompts = torch.randint(0, tcfg.vocab, (B, P), generator=g)
+    ver.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
+    gd = torch.Generator(device=device).manual_seed(11 + rank)
+    ver.fill_synthetic_kv(gd)
+    # draft: the 1B-shaped INT4 model proposes K tokens per sequence (untimed)
+    draft = LlamaModel(dcfg, device=device, seed=2000 + rank)
+    dcache = draft.make_cache(B * (math.ceil((P + K + 2) / 16) + 2) + 8, max_batch=B)
+    dr = PagedRunner(draft, dcache, list(range(B)))
+    dr.register(prompts[:, :-1].tolist())
+    for pool in (dcache.key_pool, dcache.value_pool):
+        pool.copy_(torch.randn(pool.shape, generator=gd, device=device).to(pool.dtype))
+    eng = SpeculativeEngine(dr, None, num_speculative_tokens=K, temperature=args.temperature, seed=3 + rank)
+    eng.target_runner = dr  # device lookup only
+    draft_tokens, draft_logits = eng.draft(prompts.tolist())
+    del dr, dcache, draft
+    torch.cuda.empty_cache()
+    return tcfg, target, cache, ver, draft_tokens.contiguous(), draft_logits.contiguous()
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    from cudaforge_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    tcfg, target, cache, ver, dtok, dlog = setup(args, rank, device)
+    B, K, R = args.batch, args.k, args.k + 1
+    total_steps = args.warmup + args.steps
+    gen = torch.Generator(device=device).manual_seed(99 + rank)
+    uni = torch.rand(total_steps + args.steps + 1, B, K + 1, generator=gen, device=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for i in range(args.warmup):
+        ver.step(dtok, dlog, uni[i])
+    barrier()
+    # ---- timed region (device-resident inputs) ----
+    clk = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    clk.start()
+    tokens_per_step = []
+    l0 = _lib.LAUNCHES[0]
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        res = ver.step(dtok, dlog, uni[args.warmup + i])
+        tokens_per_step.append(int((ver.n_pinned.clamp_min(0) + 1).sum()))
+    e1.record()
+    barrier()
+    clocks = clk.stop()
+    launches = _lib.LAUNCHES[0] - l0
+    ms = e0.elapsed_time(e1)
+    # ---- per-kernel timing pass (same step, CUDA events around every launch group) ----
+    kt = KernelTimer()
+    kp = max(2, min(args.steps, 4))
+    kstart = torch.cuda.Event(enable_timing=True)
+    kend = torch.cuda.Event(enable_timing=True)
+    kstart.record()
+    for i in range(kp):
+        ver.step(dtok, dlog, uni[total_steps + i], timer=kt)
+    kend.record()
+    torch.cuda.synchronize(device)
+    # ---- e2e: host inputs (pinned) -> device, results -> host, every step ----
+    h_tok = dtok.cpu().pin_memory()
+    h_uni = uni[total_steps: total_steps + args.steps].cpu().pin_memory()
+    h_out_tok = torch.empty(B, R, dtype=torch.int32).pin_memory()
+    h_out_n = torch.empty(B, dtype=torch.int32).pin_memory()
+    d_tok = torch.empty_like(dtok)
+    d_uni = torch.empty(B, K + 1, device=device)
+    barrier()
+    x0 = torch.cuda.Event(enable_timing=True)
+    x1 = torch.cuda.Event(enable_timing=True)
+    x0.record()
+    e2e_tokens = 0
+    for i in range(args.steps):
+        d_tok.copy_(h_tok, non_blocking=True)
+        d_uni.copy_(h_uni[i], non_blocking=True)
+        r = ver.step(d_tok, dlog, d_uni)
+        h_out_tok.copy_(r.tokens, non_blocking=True)
+        h_out_n.copy_(r.num_accepted, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+        e2e_tokens += int((h_out_n.clamp_min(0) + 1).sum())
+    x1.record()
+    barrier()
+    e2e_ms = x1.elapsed_time(x0) * -1 if False else x0.elapsed_time(x1)
+    h2d = dtok.numel() * 4 + B * (K + 1) * 4
+    d2h = B * R * 4 + B * 4
+
+    # max over ranks
+    t = torch.tensor([ms, e2e_ms, float(sum(tokens_per_step)), float(e2e_tokens)], device=device, dtype=torch.float64)
+    if world > 1:
+        tm = t.clone()
+        dist.all_reduce(tm[:2], op=dist.ReduceOp.MAX)
+        ts = t.clone()
+        dist.all_reduce(ts[2:], op=dist.ReduceOp.SUM)
+        ms_max, e2e_max, tok_all, e2e_tok_all = tm[0].item(), tm[1].item(), ts[2].item(), ts[3].item()
+    else:
+        ms_max, e2e_max, tok_all, e2e_tok_all = ms, e2e_ms, float(sum(tokens_per_step)), float(e2e_tokens)
+    value = tok_all / (ms_max / 1e3)
+    e2e_value = e2e_tok_all / (e2e_max / 1e3)
+
+    # roofline of the dominant kernel (W4A16 GEMM, tensor bound) and the others
+    peaks, peak_src = load_peaks()
+    M = B * R
+    gemm_flops = tcfg.gemm_flops(M)
+    gemm_ms = kt.total_ms("gemm") / kp
+    attn_ms = kt.total_ms("attn") / kp
+    other_ms = kt.total_ms("other") / kp
+    step_ms_k = kstart.elapsed_time(kend) / kp
+    achieved_tf = gemm_flops / (gemm_ms / 1e3) / 1e12
+    peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    ctx_mean = statistics.mean(ver.ctx_host)
+    attn_bytes = tcfg.layers * B * (ctx_mean + R) * tcfg.n_kv_heads * tcfg.head_dim * 2 * 2
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    traffic = None
+    tr_path = os.path.join(ROOT, "profiles", "gemm_traffic.json")
+    if os.path.exists(tr_path):
+        try:
+            traffic = json.load(open(tr_path)).get("traffic_bytes_per_step")
+        except (OSError, ValueError):
+            traffic = None
+
+    out = None
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init weights (INT4 uniform [-8,7], |N(0,0.002)| fp16 scales), random "
+                    "prompt ids, context K/V seeded random (stands in for a prefill), drafts from the random-init "
+                    "1B INT4 draft model",
+            "config": {"workload": "cfg3 8B-INT4 verify+accept", "model": "Llama-3-8B-shaped W4A16 g128",
+                       "draft": "1B-shaped W4A16 (excluded from timing)", "global_batch": B * world,
+                       "batch_per_gpu": B, "seq_len": args.ctx, "k": K, "temperature": args.temperature,
+                       "parallelism": f"batch-sharded dp{world} (no collective)",
+                       "l2": "inputs larger than L2 (3.9 GB weights + KV pools per GPU)",
+                       "mean_accepted_per_seq_step": round(tok_all / (args.steps * B * world) - 1, 3)},
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "roofline": {"bound": "tensor", "kernel": "w4a16_gemm (tcgen05, all 129 GEMMs of a step)",
+                         "achieved": round(achieved_tf, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": round(achieved_tf / peak_tf, 4), "traffic": traffic,
+                         "peak_source": f"{peak_src} bf16_tflops_sustained",
+                         "algorithmic_flops_per_step": gemm_flops, "gemm_ms_per_step": round(gemm_ms, 3)},
+            "kernels": {
+                "step_ms_instrumented": round(step_ms_k, 3),
+                "gemm_ms": round(gemm_ms, 3), "attn_ms": round(attn_ms, 3), "other_ms": round(other_ms, 3),
+                "attention": {"bound": "hbm", "bytes_per_step": attn_bytes,
+                              "achieved_gbs": round(attn_bytes / (attn_ms / 1e3) / 1e9, 1),
+                              "peak_gbs": hbm, "frac": round(attn_bytes / (attn_ms / 1e3) / 1e9 / hbm, 4)},
+            },
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+# ---------------------------------------------------------------- CPU baseline / reference arm
+def cpu_step_sample(args, threads: int):
+    """One bounded CPU sample of the verify+accept step at the bench shapes:
+    one transformer layer of the 8B-shaped model (torch fp32 on the host,
+    weights dequantised from INT4) over the 64 x 6 verify rows with a
+    1024-token context, the lm_head, and the acceptance of all sequences by
+    the reference's own compiled verify_candidates (oracle/_ref) fed the
+    fp32 softmaxes, or the oracle restatement when that build is absent.
+    Returns (seconds for a full step extrapolated to 32 layers, accepted
+    tokens of the step, description)."""
+    import numpy as np
+
+    import oracle
+
+    torch.set_num_threads(threads)
+    from cudaforge_b200.model import LLAMA_8B
+    c = LLAMA_8B
+    B, K, P = args.batch, args.k, args.ctx
+    R = K + 1
+    M = B * R
+    g = torch.Generator().manual_seed(5)
+
+    def w4(n, k):
+        q = torch.randint(0, 16, (k, n), generator=g, dtype=torch.int8).float() - 8.0
+        s = (torch.randn(k // 128, n, generator=g).abs() * 0.002).half().float().repeat_interleave(128, 0)
+        return (q * s).T.contiguous()  # [n, k] fp32
+
+    W = {name: w4(n, k) for name, n, k in c.linear_shapes()}
+    x = torch.randn(M, c.d_model, generator=g) * 0.02
+    kc = torch.randn(B, P, c.n_kv_heads, c.head_dim, generator=g)
+    vc = torch.randn(B, P, c.n_kv_heads, c.head_dim, generator=g)
+    from oracle import llama_ref
+    t0 = time.perf_counter()
+    xn = llama_ref.rmsnorm(x, torch.ones(c.d_model))
+    qkv = xn @ W["qkv"].T
+    q = qkv[:, : c.n_heads * c.head_dim].view(B, R, c.n_heads, c.head_dim)
+    kn = qkv[:, c.n_heads * c.head_dim:(c.n_heads + c.n_kv_heads) * c.head_dim].view(B, R, c.n_kv_heads, c.head_dim)
+    vn = qkv[:, (c.n_heads + c.n_kv_heads) * c.head_dim:].view(B, R, c.n_kv_heads, c.head_dim)
+    G = c.n_heads // c.n_kv_heads
+    k_all = torch.cat([kc, kn], 1).repeat_interleave(G, 2)
+    v_all = torch.cat([vc, vn], 1).repeat_interleave(G, 2)
+    s = torch.einsum("brhd,bthd->bhrt", q, k_all) / math.sqrt(c.head_dim)
+    mask = torch.ones(R, P + R, dtype=torch.bool)
+    mask[:, P:] = torch.tril(torch.ones(R, R, dtype=torch.bool))
+    s = s.masked_fill(~mask, float("-inf"))
+    a = torch.einsum("bhrt,bthd->brhd", torch.softmax(s, -1), v_all).reshape(M, -1)
+    x = x + a @ W["o"].T
+    xn = llama_ref.rmsnorm(x, torch.ones(c.d_model))
+    gu = xn @ W["gate_up"].T
+    x = x + (torch.nn.functional.silu(gu[:, : c.ffn]) * gu[:, c.ffn:]) @ W["down"].T
+    t_layer = time.perf_counter() - t0
+    del W
+    lm = torch.randn(c.vocab, c.d_model, generator=g) * 0.007
+    t1 = time.perf_counter()
+    logits = (llama_ref.rmsnorm(x, torch.ones(c.d_model)) @ lm.T).view(B, R, c.vocab)
+    t_lm = time.perf_counter() - t1
+    del lm
+    # acceptance: softmax(/T) of the target rows and K draft rows, then verify_candidates per sequence
+    dl = (logits[:, :K] + torch.randn(B, K, c.vocab, generator=g) * 0.5).numpy()
+    tl = logits.numpy()
+    dt = np.stack([np.argmax(dl[b], -1) for b in range(B)]).astype(np.int32)
+    u = torch.rand(B, K + 1, generator=g).numpy()
+    t2 = time.perf_counter()
+    dp = oracle.softmax_rows(dl, args.temperature)
+    tp = oracle.softmax_rows(tl, args.temperature)
+    tokens = 0
+    if oracle.ref_available():
+        from concurrent.futures import ThreadPoolExecutor
+
+        def one(b):
+            tok, na, ef = oracle.ref_verify(42 + b, dt[b], dp[b], tp[b], -1)
+            return na + 1
+
+        with ThreadPoolExecutor(max_workers=threads) as ex:
+            tokens = sum(ex.map(one, range(B)))
+        kind_acc = "reference verify_candidates (compiled from the reference sources)"
+    else:
+        tok, na, ef = oracle.accept(dt, dp, tp, u, -1)
+        tokens = int((na + 1).sum())
+        kind_acc = "oracle restatement of verify_candidates"
+    t_acc = time.perf_counter() - t2
+    step_s = c.layers * t_layer + t_lm + t_acc
+    desc = (f"1 of {c.layers} layers at M={M} rows (ctx {P}) timed and x{c.layers}, + lm_head + acceptance of "
+            f"{B} seqs ({kind_acc}); forward is the torch fp32 restatement (the reference has no model forward)")
+    return step_s, tokens, desc, {"layer_s": t_layer, "lm_head_s": t_lm, "accept_s": t_acc}
+
+
+def run_reference(args):
+    """--impl reference: the reference path's CPU implementation on the host
+    cores (rank 0 only; other ranks exit without work)."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    samples = []
+    toks = []
+    for i in range(args.warmup + args.steps):
+        s, t, desc, parts = cpu_step_sample(args, threads)
+        if i >= args.warmup:
+            samples.append(s)
+            toks.append(t)
+    tot_s = sum(samples)
+    value = sum(toks) / tot_s
+    return {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * tot_s / args.steps, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "cfg3 8B-INT4 verify+accept", "batch": args.batch,
+                                            "seq_len": args.ctx, "k": args.k},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def run_case(args):
+    """Single-kernel cases at the bench shapes (for ncu captures and per-shape
+    timing); prints one JSON line per shape."""
+    from cudaforge_b200 import ops
+    from cudaforge_b200.gemm import w4a16_gemm
+    from cudaforge_b200.model import LLAMA_8B
+    dev = torch.device("cuda", 0)
+    c = LLAMA_8B
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.case == "gemm":
+        M = args.batch * (args.k + 1)
+        shapes = [(n, k) for _, n, k in c.linear_shapes()] + [(c.vocab, c.d_model)]
+        if args.shape:
+            shapes = [tuple(int(v) for v in args.shape.split("x"))]
+        x = (torch.randn(M, 14336, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        for n, k in shapes:
+            wq = torch.randint(-2**31, 2**31 - 1, (k // 8, n), generator=g, device=dev, dtype=torch.int32)
+            sc = (torch.randn(k // 128, n, generator=g, device=dev).abs() * 0.002).half()
+            y = torch.empty(M, n, dtype=torch.bfloat16, device=dev)
+            xs = x[:, :k]
+            for _ in range(2):
+                w4a16_gemm(xs, wq, sc, out=y)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.iters):
+                w4a16_gemm(xs, wq, sc, out=y)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.iters
+            print(json.dumps({"case": "w4a16_gemm", "M": M, "N": n, "K": k, "us": round(ms * 1e3, 1),
+                              "tflops": round(2 * M * n * k / (ms / 1e3) / 1e12, 1),
+                              "weight_gbs": round(n * k * (0.5 + 2 / 128) / (ms / 1e3) / 1e9, 1)}), flush=True)
+    elif args.case == "attention":
+        from cudaforge_b200.kv_cache import KVCacheConfig, PagedKVCache
+        B, R, P = args.batch, args.k + 1, args.ctx
+        bps = math.ceil((P + R) / 16) + 1
+        cfg = KVCacheConfig(num_layers=1, num_kv_heads=c.n_kv_heads, head_dim=c.head_dim, block_size=16,
+                            total_gpu_blocks=B * bps + 4, enable_prefix_caching=False, max_supported_batch_size=B)
+        cache = PagedKVCache(cfg)
+        for i in range(B):
+            cache.register_sequence_with_prefix(i, list(range(P)))
+        tables, ctx = cache.prepare_batch_metadata(list(range(B)))
+        q = torch.randn(B * R, c.n_heads * c.head_dim, generator=g, device=dev).to(torch.bfloat16)
+        kn = torch.randn(B, R, c.n_kv_heads, c.head_dim, generator=g, device=dev).to(torch.bfloat16)
+        vn = torch.randn_like(kn)
+        out = torch.empty_like(q)
+        for _ in range(2):
+            ops.verify_attention(cache, 0, q, kn, vn, tables, ctx, P, rows=R, num_q_heads=c.n_heads, out=out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            ops.verify_attention(cache, 0, q, kn, vn, tables, ctx, P, rows=R, num_q_heads=c.n_heads, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.iters
+        byts = B * (P + R) * c.n_kv_heads * c.head_dim * 2 * 2
+        print(json.dumps({"case": "verify_attention", "B": B, "ctx": P, "R": R, "us": round(ms * 1e3, 1),
+                          "gbs": round(byts / (ms / 1e3) / 1e9, 1)}), flush=True)
+    elif args.case == "accept":
+        from cudaforge_b200.accept import accept_sample
+        B, K, V = args.batch, args.k, c.vocab
+        d = (torch.randn(B, K, V, generator=g, device=dev) * 2).to(torch.bfloat16)
+        t = (torch.randn(B, K + 1, V, generator=g, device=dev) * 2).to(torch.bfloat16)
+        dt = torch.randint(0, V, (B, K), generator=g, device=dev, dtype=torch.int32)
+        u = torch.rand(B, K + 1, generator=g, device=dev)
+        for _ in range(2):
+            accept_sample(d, t, dt, u)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            accept_sample(d, t, dt, u)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.iters
+        byts = B * (2 * K + 1) * V * 2
+        print(json.dumps({"case": "accept", "B": B, "K": K, "V": V, "us": round(ms * 1e3, 1),
+                          "gbs": round(byts / (ms / 1e3) / 1e9, 1)}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="8b", choices=["8b", "tiny"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ctx", type=int, default=1024)
+    ap.add_argument("--k", type=int, default=5)
+    ap.add_argument("--temperature", type=float, default=1.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default=None, choices=["gemm", "attention", "accept"],
+                    help="time a single kernel at the bench shapes (profiling aid)")
+    ap.add_argument("--shape", default=None, help="NxK for --case gemm")
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
+    if args.impl == "reference":
+        out = run_reference(args)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+    out = run_ours(args)
+    if out is not None:
+        if out["n_gpus"] == 1 and not args.no_cpu_baseline and args.config == "8b":
+            s, t, desc, parts = cpu_step_sample(args, 1)
+            out["cpu_baseline"] = {"value": round(t / s, 3), "unit": UNIT, "cores": 1, "kind": "port",
+                                   "sample": desc, "parts_s": {k: round(v, 3) for k, v in parts.items()}}
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -75,6 +75,13 @@ def build() -> None:
 
 _lib = None
 
+# Kernel launches issued through this binding (for the bench's gpu_launches claim).
+LAUNCHES = [0]
+
+
+def count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
 
 def lib() -> ctypes.CDLL:
     global _lib

@@ -125,4 +125,5 @@ def accept_sample(
     s = stream if stream is not None else torch.cuda.current_stream(dev)
     with torch.cuda.device(dev):
         _lib.check(L.cf_accept_sample(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), "cf_accept_sample")
+    _lib.count(3 if export_probs else 2)
     return out

@@ -227,6 +227,16 @@ extern "C" int cf_kvcache_append_tokens(cf_kvcache *h, uint64_t seq, uint32_t n)
   return CF_OK;
 }
 
+extern "C" int cf_kvcache_append_batch(cf_kvcache *h, const uint64_t *seqs, const int32_t *n, uint32_t batch) {
+  if (!h || (batch && (!seqs || !n))) return CF_EINVAL;
+  for (uint32_t i = 0; i < batch; ++i) {  // batch order == the reference's per-call order
+    if (n[i] <= 0) continue;
+    const int rc = cf_kvcache_append_tokens(h, seqs[i], (uint32_t)n[i]);
+    if (rc != CF_OK) return rc;
+  }
+  return CF_OK;
+}
+
 extern "C" int cf_kvcache_unregister_sequence(cf_kvcache *h, uint64_t seq) {
   if (!h) return CF_EINVAL;
   Cache &c = h->c;

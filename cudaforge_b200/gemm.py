@@ -45,6 +45,7 @@ def repack_int4(wq: torch.Tensor, stream=None) -> torch.Tensor:
     s = stream or torch.cuda.current_stream(wq.device)
     _lib.check(_lib.lib().cf_w4a16_repack(ctypes.c_void_p(wq.data_ptr()), ctypes.c_void_p(out.data_ptr()),
                                           Kp * 8, N, ctypes.c_void_p(s.cuda_stream)), "cf_w4a16_repack")
+    _lib.count()
     return out
 
 
@@ -81,6 +82,7 @@ def _gemm(fn, x, w, scales, n, residual, out, split_k, workspace, status, int4, 
                         timeout_ns=timeout_ns)
     s = stream or torch.cuda.current_stream(x.device)
     _lib.check(fn(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), fn.__name__)
+    _lib.count(2 if need else 1)
     return out
 
 

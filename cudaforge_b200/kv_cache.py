@@ -102,6 +102,7 @@ def _lib_kv():
         L.cf_kvcache_destroy.argtypes = [_P]
         L.cf_kvcache_register_sequence.argtypes = [_P, ctypes.c_uint64, _P, ctypes.c_uint32, _P]
         L.cf_kvcache_append_tokens.argtypes = [_P, ctypes.c_uint64, ctypes.c_uint32]
+        L.cf_kvcache_append_batch.argtypes = [_P, _P, _P, ctypes.c_uint32]
         L.cf_kvcache_unregister_sequence.argtypes = [_P, ctypes.c_uint64]
         L.cf_kvcache_fork_sequence.argtypes = [_P, ctypes.c_uint64, ctypes.c_uint64]
         L.cf_kvcache_get_block_table.argtypes = [_P, ctypes.c_uint64, _P, ctypes.c_uint32, _P]
@@ -168,6 +169,23 @@ class PagedKVCache:
 
     def append_tokens(self, sequence_id: int, num_tokens: int = 1) -> None:
         self._check(_lib_kv().cf_kvcache_append_tokens(self._h, sequence_id, num_tokens), "append_tokens")
+
+    def append_batch(self, sequence_ids: Sequence[int], counts) -> None:
+        """append_tokens(sequence_ids[i], counts[i]) for every i in order (counts <= 0 skipped)."""
+        B = len(sequence_ids)
+        ids = (ctypes.c_uint64 * max(1, B))(*sequence_ids)
+        n = (ctypes.c_int32 * max(1, B))(*[int(x) for x in counts])
+        self._check(_lib_kv().cf_kvcache_append_batch(self._h, ids, n, B), "append_tokens")
+
+    def prepare_batch_into(self, sequence_ids: Sequence[int], tables: torch.Tensor, ctx: torch.Tensor) -> int:
+        """prepare_batch_metadata into caller (pinned) CPU buffers: tables is a
+        flat int32 buffer, filled as [B, max_blocks]; returns max_blocks."""
+        B = len(sequence_ids)
+        ids = (ctypes.c_uint64 * max(1, B))(*sequence_ids)
+        mb = ctypes.c_uint32(0)
+        self._check(_lib_kv().cf_kvcache_prepare_batch(self._h, ids, B, tables.data_ptr(), tables.numel(),
+                                                       ctx.data_ptr(), ctypes.byref(mb)), "prepare_batch_metadata")
+        return mb.value
 
     def unregister_sequence(self, sequence_id: int) -> None:
         self._check(_lib_kv().cf_kvcache_unregister_sequence(self._h, sequence_id), "unregister_sequence")

@@ -84,6 +84,18 @@ class Linear:
         return dense_gemm(x, self.w, out=out, residual=residual, workspace=workspace)
 
 
+class _NullCtx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def _null_timer(kind):
+    return _NullCtx()
+
+
 class LlamaModel:
     """Random-init Llama-shaped model (seeded), resident on one device."""
 
@@ -126,31 +138,46 @@ class LlamaModel:
 
     def forward_rows(self, cache, tokens: torch.Tensor, positions: torch.Tensor, block_tables: torch.Tensor,
                      context_lens: torch.Tensor, max_context: int, tree_mask: Optional[torch.Tensor] = None,
-                     status: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     status: Optional[torch.Tensor] = None, timer=None) -> torch.Tensor:
         """tokens [B, R] int32 (row 0 = last emitted token, then drafts / tree
         nodes), positions [B*R] int32, block tables / context lengths from the
         cache (context = tokens already in the pool).  Returns logits [B*R, V]
-        (a reused buffer) and leaves this step's K/V rows in buffers()["k_new"/"v_new"]."""
+        (a reused buffer) and leaves this step's K/V rows in buffers()["k_new"/"v_new"].
+        `timer(kind)` (optional) returns a context manager wrapped around each
+        launch group ("gemm", "attn", "other") for per-kernel timing."""
         c = self.cfg
         B, R = tokens.shape
         bf = self.buffers(B, R)
         h, xn, qkv, attn, gu, act = bf["h"], bf["xn"], bf["qkv"], bf["attn"], bf["gu"], bf["act"]
-        ops.embedding(tokens.reshape(-1), self.embed, out=h)
+        T = timer or _null_timer
+        with T("other"):
+            ops.embedding(tokens.reshape(-1), self.embed, out=h)
         for li, lay in enumerate(self.layers):
-            ops.rmsnorm(h, lay["attn_norm"], c.eps, out=xn)
-            lay["qkv"](xn, out=qkv)
-            ops.rope_qkv(qkv, positions, c.n_heads, c.n_kv_heads, c.head_dim, bf["k_new"][li], bf["v_new"][li],
-                         base=c.rope_base)
-            ops.verify_attention(cache, li, qkv, bf["k_new"][li], bf["v_new"][li], block_tables, context_lens,
-                                 max_context, rows=R, num_q_heads=c.n_heads, out=attn, tree_mask=tree_mask,
-                                 status=status)
-            lay["o"](attn, out=h, residual=h)
-            ops.rmsnorm(h, lay["ffn_norm"], c.eps, out=xn)
-            lay["gate_up"](xn, out=gu)
-            ops.silu_mul(gu, c.ffn, out=act)
-            lay["down"](act, out=h, residual=h)
-        ops.rmsnorm(h, self.final_norm, c.eps, out=xn)
-        self.lm_head(xn, out=bf["logits"])
+            with T("other"):
+                ops.rmsnorm(h, lay["attn_norm"], c.eps, out=xn)
+            with T("gemm"):
+                lay["qkv"](xn, out=qkv)
+            with T("other"):
+                ops.rope_qkv(qkv, positions, c.n_heads, c.n_kv_heads, c.head_dim, bf["k_new"][li], bf["v_new"][li],
+                             base=c.rope_base)
+            with T("attn"):
+                ops.verify_attention(cache, li, qkv, bf["k_new"][li], bf["v_new"][li], block_tables, context_lens,
+                                     max_context, rows=R, num_q_heads=c.n_heads, out=attn, tree_mask=tree_mask,
+                                     status=status)
+            with T("gemm"):
+                lay["o"](attn, out=h, residual=h)
+            with T("other"):
+                ops.rmsnorm(h, lay["ffn_norm"], c.eps, out=xn)
+            with T("gemm"):
+                lay["gate_up"](xn, out=gu)
+            with T("other"):
+                ops.silu_mul(gu, c.ffn, out=act)
+            with T("gemm"):
+                lay["down"](act, out=h, residual=h)
+        with T("other"):
+            ops.rmsnorm(h, self.final_norm, c.eps, out=xn)
+        with T("gemm"):
+            self.lm_head(xn, out=bf["logits"])
         return bf["logits"]
 
     def make_cache(self, total_blocks: int, max_batch: int = 256, max_blocks_per_seq: int = 512,

@@ -65,6 +65,7 @@ def verify_attention(cache, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_
         ws = _Ws.get("attn", q.device, need)
         a.workspace, a.workspace_bytes = ws.data_ptr(), need
     _lib.check(L.cf_verify_attention(ctypes.byref(a), _s(stream, q.device)), "cf_verify_attention")
+    _lib.count(2 if need else 1)
     return out
 
 
@@ -80,6 +81,7 @@ def kv_commit(cache, k_new: torch.Tensor, v_new: torch.Tensor, n_commit: torch.T
                             block_tables=block_tables.data_ptr(), max_blocks=block_tables.shape[1],
                             status=_ptr(status))
     _lib.check(_lib.lib().cf_kv_commit(ctypes.byref(a), _s(stream, k_new.device)), "cf_kv_commit")
+    _lib.count()
 
 
 def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None):
@@ -88,6 +90,7 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor
         out = torch.empty((m, table.shape[1]), dtype=table.dtype, device=table.device)
     _lib.check(_lib.lib().cf_embedding(ids.data_ptr(), m, table.data_ptr(), table.shape[0], table.shape[1],
                                        out.data_ptr(), _DT[table.dtype], _s(stream, table.device)), "cf_embedding")
+    _lib.count()
     return out
 
 
@@ -96,6 +99,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: Optional[t
         out = torch.empty_like(x)
     _lib.check(_lib.lib().cf_rmsnorm(x.data_ptr(), x.stride(0), w.data_ptr(), out.data_ptr(), out.stride(0),
                                      x.shape[0], x.shape[1], eps, _DT[x.dtype], _s(stream, x.device)), "cf_rmsnorm")
+    _lib.count()
     return out
 
 
@@ -104,6 +108,7 @@ def rope_qkv(qkv: torch.Tensor, pos: torch.Tensor, num_q_heads: int, num_kv_head
     _lib.check(_lib.lib().cf_rope_qkv(qkv.data_ptr(), qkv.stride(0), qkv.shape[0], num_q_heads, num_kv_heads,
                                       head_dim, pos.data_ptr(), base, k_new.data_ptr(), v_new.data_ptr(),
                                       _DT[qkv.dtype], _s(stream, qkv.device)), "cf_rope_qkv")
+    _lib.count()
 
 
 def silu_mul(gu: torch.Tensor, ffn: int, out: Optional[torch.Tensor] = None, stream=None):
@@ -111,4 +116,5 @@ def silu_mul(gu: torch.Tensor, ffn: int, out: Optional[torch.Tensor] = None, str
         out = torch.empty((gu.shape[0], ffn), dtype=gu.dtype, device=gu.device)
     _lib.check(_lib.lib().cf_silu_mul(gu.data_ptr(), gu.stride(0), out.data_ptr(), out.stride(0), gu.shape[0], ffn,
                                       _DT[gu.dtype], _s(stream, gu.device)), "cf_silu_mul")
+    _lib.count()
     return out

@@ -1,0 +1,114 @@
+"""BatchVerifier: the device-resident verify + accept + commit step.
+
+This is the hot path of one speculative-decoding round for a fixed batch of
+sequences (the work cudaforge/speculative.py:136-195 does per step, with the
+reference's native acceptance semantics, speculative.cpp:50-103):
+
+  1. target verify forward over R = K+1 rows per sequence (row 0 = the last
+     emitted token, rows 1..K = the drafts) against the paged KV cache;
+  2. fused acceptance sampling on the target / draft logits;
+  3. commit: the page tables grow by num_accepted+1 tokens per sequence in
+     batch order (cf_kvcache_append_batch, reference PagedKVCache semantics),
+     the new tables go to the device, and cf_kv_commit copies the accepted
+     rows' K/V of every layer into the pool.
+
+All per-step state (token rows, positions, context lengths, block tables,
+acceptance outputs) lives in preallocated device buffers; the only host
+round trip is the num_accepted read-back the page tables need.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+
+from . import ops
+from .accept import AcceptResult, accept_sample
+from .model import LlamaModel
+
+
+class BatchVerifier:
+    def __init__(self, model: LlamaModel, cache, seq_ids: Sequence[int], k: int, *, temperature: float = 1.0,
+                 greedy: bool = False, eos_token_id: int = -1, max_blocks_per_seq: int = 512):
+        self.model, self.cache = model, cache
+        self.seq_ids = list(seq_ids)
+        self.B, self.K, self.R = len(self.seq_ids), k, k + 1
+        self.temperature, self.greedy, self.eos = max(temperature, 1e-5), greedy, eos_token_id
+        dev = model.device
+        B, R = self.B, self.R
+        self.tokens = torch.zeros(B, R, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(B * R, dtype=torch.int32, device=dev)
+        self.ctx = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.ctx_host = [0] * B
+        self.ar = torch.arange(R, dtype=torch.int32, device=dev).view(1, R)
+        self.tables_pinned = torch.full((B * max_blocks_per_seq,), -1, dtype=torch.int32).pin_memory()
+        self.ctx_pinned = torch.zeros(B, dtype=torch.int32).pin_memory()
+        self.tables_dev = torch.full((B * max_blocks_per_seq,), -1, dtype=torch.int32, device=dev)
+        self.max_blocks = 0
+        self.n_pinned = torch.zeros(B, dtype=torch.int32).pin_memory()
+        self.res = AcceptResult(tokens=torch.zeros(B, R, dtype=torch.int32, device=dev),
+                                num_accepted=torch.zeros(B, dtype=torch.int32, device=dev),
+                                eos=torch.zeros(B, dtype=torch.bool, device=dev))
+        self.ws = torch.empty(4096 + 16 * B * (2 * k + 1), dtype=torch.uint8, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.model.buffers(B, R)
+
+    # ---- state ----
+    def _upload_tables(self, stream=None):
+        self.max_blocks = self.cache.prepare_batch_into(self.seq_ids, self.tables_pinned, self.ctx_pinned)
+        n = self.B * self.max_blocks
+        self.tables_dev[:n].copy_(self.tables_pinned[:n], non_blocking=True)
+
+    def tables(self) -> torch.Tensor:
+        return self.tables_dev[: self.B * self.max_blocks].view(self.B, self.max_blocks)
+
+    def register_context(self, prompts, last_tokens) -> None:
+        """Register each sequence's cached prompt (page tables) and set row 0
+        (the last emitted token, not yet cached).  Pool contents come from a
+        prefill or from fill_synthetic_kv()."""
+        for sid, p in zip(self.seq_ids, prompts):
+            self.cache.register_sequence_with_prefix(sid, p)
+        self.ctx_host = [len(p) for p in prompts]
+        self.ctx.copy_(torch.tensor(self.ctx_host, dtype=torch.int32))
+        self.tokens[:, 0].copy_(torch.as_tensor(last_tokens, dtype=torch.int32))
+        self._upload_tables()
+
+    def fill_synthetic_kv(self, gen: torch.Generator, std: float = 1.0) -> None:
+        """Seeded random K/V for every pool slot (stands in for a prefill of
+        random prompts: the verify step reads the same bytes either way)."""
+        for pool in (self.cache.key_pool, self.cache.value_pool):
+            flat = pool.view(-1)
+            chunk = 1 << 28
+            for i in range(0, flat.numel(), chunk):
+                seg = flat[i: i + chunk]
+                seg.copy_((torch.randn(seg.numel(), generator=gen, device=seg.device) * std).to(seg.dtype))
+
+    # ---- the step ----
+    @torch.no_grad()
+    def step(self, draft_tokens: torch.Tensor, draft_logits: Optional[torch.Tensor],
+             uniforms: Optional[torch.Tensor], timer=None) -> AcceptResult:
+        """draft_tokens [B, K] int32 and draft_logits [B, K, V] (device),
+        uniforms [B, K+1] fp32 (device; unused when greedy).  Returns the
+        acceptance result (device tensors, reused across steps)."""
+        B, R = self.B, self.R
+        self.tokens[:, 1:].copy_(draft_tokens)
+        torch.add(self.ctx.view(B, 1), self.ar, out=self.pos.view(B, R))
+        logits = self.model.forward_rows(self.cache, self.tokens, self.pos, self.tables(), self.ctx,
+                                         max(self.ctx_host), status=self.status, timer=timer)
+        res = accept_sample(draft_logits, logits.view(B, R, -1), draft_tokens, uniforms,
+                            temperature=self.temperature, eos_token_id=self.eos, greedy=self.greedy,
+                            workspace=self.ws, out=self.res)
+        self.n_pinned.copy_(res.num_accepted, non_blocking=True)
+        torch.cuda.current_stream(self.model.device).synchronize()
+        n = [max(0, int(x)) + 1 for x in self.n_pinned.tolist()]
+        start = self.ctx.clone()
+        self.cache.append_batch(self.seq_ids, n)
+        self._upload_tables()
+        ops.kv_commit(self.cache, self.model.buffers(B, R)["k_new"], self.model.buffers(B, R)["v_new"],
+                      res.num_accepted, start, self.tables(), n_commit_add=1, status=self.status)
+        # next round: context grows by n, row 0 = the final token
+        self.ctx.add_(res.num_accepted.clamp_min(0) + 1)
+        self.ctx_host = [c + x for c, x in zip(self.ctx_host, n)]
+        idx = res.num_accepted.clamp_min(0).long().view(B, 1)
+        self.tokens[:, :1].copy_(res.tokens.gather(1, idx))
+        return res

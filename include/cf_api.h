@@ -207,6 +207,10 @@ int cf_kvcache_register_sequence(cf_kvcache *h, uint64_t seq, const int32_t *tok
                                  uint32_t *matched_out);
 /* append_tokens (:255-286) */
 int cf_kvcache_append_tokens(cf_kvcache *h, uint64_t seq, uint32_t n);
+/* append_tokens for seqs[i] with n[i] tokens (n <= 0 skipped), in index
+ * order -- the engine's per-token commit loop (cudaforge/engine.py:222-224)
+ * in one call; stops at the first error. */
+int cf_kvcache_append_batch(cf_kvcache *h, const uint64_t *seqs, const int32_t *n, uint32_t batch);
 /* unregister_sequence (:288-299) */
 int cf_kvcache_unregister_sequence(cf_kvcache *h, uint64_t seq);
 /* fork_sequence (:301-316) */
