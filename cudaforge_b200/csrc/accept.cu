@@ -21,13 +21,13 @@
 // the value a decision sees is the value the parity export writes.
 #include "common.cuh"
 
+#include <limits.h>
 #include <math.h>
 
 namespace {
 
 constexpr int kStatsThreads = 512;
-constexpr int kDecideThreads = 256;  // warp 0 runs the serial chain, warps 1-7 produce
-constexpr int kChunk = 2048;         // elements per double-buffered chunk
+constexpr int kDecideThreads = 512;
 
 struct RowStat {
   float mc;  // max_i fl(x_i * c)
@@ -38,6 +38,26 @@ template <typename T>
 __device__ __forceinline__ const T *row_ptr(const void *base, int64_t seq_stride,
                                             int64_t row_stride, int b, int r) {
   return reinterpret_cast<const T *>(base) + (int64_t)b * seq_stride + (int64_t)r * row_stride;
+}
+
+// Eight consecutive logits as floats (16-B vector load when aligned).
+template <typename T>
+__device__ __forceinline__ void load8(const T *x, int64_t i0, int64_t V, float (&o)[8]) {
+  const T *p = x + i0;
+  if (i0 + 8 <= V && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    if constexpr (sizeof(T) == 2) {
+      cf::Vec16<T> pk;
+      pk.raw = *reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = pk.get(j);
+    } else {
+      const float4 a = reinterpret_cast<const float4 *>(p)[0], b = reinterpret_cast<const float4 *>(p)[1];
+      o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = (i0 + j < V) ? cf::to_float(p[j]) : 0.0f;
+  }
 }
 
 __device__ __forceinline__ float prob_of(float x, float c, RowStat st) {
@@ -146,105 +166,217 @@ __global__ void export_probs_kernel(cf_accept_args a, float c, const RowStat *st
 }
 
 // ---------------------------------------------------------------------------
-// Pass 2 helpers: the reference's sequential fp32 chains, run by one thread
-// over double-buffered chunks that warps 1-7 fill in parallel.
+// Pass 2: the reference's sequential fp32 accumulation, computed exactly in
+// parallel.
+//
+// The reference accumulates `cum += v_i` left to right in fp32
+// (speculative.cpp:16-21, :34-35).  All v_i here are >= 0, so cum never
+// decreases.  While cum stays inside one binade [2^e, 2^(e+1)) (ulp u = 2^ue,
+// ue = max(e, -126) - 23) every partial sum is an integer multiple C*u with
+// C < 2^24, and fl(C*u + v) = (C + inc)*u where inc is v/u rounded to nearest,
+// ties to the even RESULT: the increment depends on v and on C's parity only.
+// Each element is therefore a map on (C mod 2) -> increment, and maps compose
+// associatively: a block-wide scan of these maps gives every exact partial
+// sum of a chunk at once.  An element whose sum leaves the binade (or meets a
+// NaN / Inf) is applied directly in fp32 by the thread that owns it and the
+// chunk resumes after it; the binade index only grows, so this happens a few
+// dozen times per row at most.  The result is bit-identical to the serial
+// loop.
 // ---------------------------------------------------------------------------
-struct ChainShared {
-  float buf[2][kChunk];
-  int64_t found;
-  float total;
+constexpr int kScanThreads = 512;
+constexpr int kPerThread = 8;
+constexpr int kScanChunk = kScanThreads * kPerThread;
+constexpr int kSat = 1 << 26;
+constexpr int kTop = 1 << 24;
+
+struct IncMap {
+  int e, o;  // ulps added when the running integer is even / odd
 };
 
-// Returns the fp32 sum  ((v0 + v1) + v2) + ...  in index order.
-template <class F>
-__device__ float serial_sum(F f, int64_t V, ChainShared &sh) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t nch = (V + kChunk - 1) / kChunk;
-  auto fill = [&](int64_t ch) {
-    const int64_t base = ch * kChunk;
-    const int n = (int)((V - base) < kChunk ? (V - base) : kChunk);
-    float *dst = sh.buf[ch & 1];
-    for (int j = tid - 32; j < n; j += kDecideThreads - 32) dst[j] = f(base + j);
-  };
-  if (warp != 0) fill(0);
-  float acc = 0.0f;
-  __syncthreads();
-  for (int64_t ch = 0; ch < nch; ++ch) {
-    if (warp != 0) {
-      if (ch + 1 < nch) fill(ch + 1);
-    } else if (lane == 0) {
-      const int n = (int)((V - ch * kChunk) < kChunk ? (V - ch * kChunk) : kChunk);
-      const float *src = sh.buf[ch & 1];
-      int j = 0;
-      for (; j + 4 <= n; j += 4) {
-        float4 v = *reinterpret_cast<const float4 *>(src + j);
-        acc = __fadd_rn(acc, v.x);
-        acc = __fadd_rn(acc, v.y);
-        acc = __fadd_rn(acc, v.z);
-        acc = __fadd_rn(acc, v.w);
-      }
-      for (; j < n; ++j) acc = __fadd_rn(acc, src[j]);
-    }
-    __syncthreads();
-  }
-  if (tid == 0) sh.total = acc;
-  __syncthreads();
-  float t = sh.total;
-  __syncthreads();
-  return t;
+__device__ __forceinline__ int sat_add(int a, int b) { return min(a + b, kSat); }
+
+// f, then g
+__device__ __forceinline__ IncMap compose(IncMap f, IncMap g) {
+  IncMap r;
+  r.e = sat_add(f.e, (f.e & 1) ? g.o : g.e);
+  r.o = sat_add(f.o, ((1 + f.o) & 1) ? g.o : g.e);
+  return r;
 }
 
-// Returns the first index i with r <= (v0 + ... + vi) (sequential fp32), or
-// V-1 when no prefix reaches r.
-template <class F>
-__device__ int64_t serial_search(F f, int64_t V, float r, ChainShared &sh) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t nch = (V + kChunk - 1) / kChunk;
-  auto fill = [&](int64_t ch) {
-    const int64_t base = ch * kChunk;
-    const int n = (int)((V - base) < kChunk ? (V - base) : kChunk);
-    float *dst = sh.buf[ch & 1];
-    for (int j = tid - 32; j < n; j += kDecideThreads - 32) dst[j] = f(base + j);
-  };
-  if (tid == 0) sh.found = -1;
-  if (warp != 0) fill(0);
-  float cum = 0.0f;
+__device__ __forceinline__ int apply(IncMap f, int C) { return C + ((C & 1) ? f.o : f.e); }
+
+// The increment map of adding v (>= 0) on the ulp grid 2^ue.  Values the grid
+// model cannot represent (NaN, Inf, or a jump past the binade) saturate,
+// which forces the direct fp32 path.
+__device__ __forceinline__ IncMap elem_map(float v, int ue) {
+  const uint32_t bits = __float_as_uint(v);
+  const int ex = (bits >> 23) & 0xff;
+  uint32_t m = bits & 0x7fffffu;
+  if (ex == 0xff) return {kSat, kSat};
+  if (ex) m |= 0x800000u;
+  if (m == 0) return {0, 0};
+  const int ulp_v = (ex ? ex : 1) - 127 - 23;
+  const int s = ue - ulp_v;  // v / u = m * 2^-s
+  if (s <= 0) {
+    if (-s >= 3) return {kSat, kSat};
+    const int A = (int)(m << (-s));
+    return {A, A};
+  }
+  if (s >= 25) return {0, 0};  // v < u/2
+  const uint32_t fl = m >> s, rem = m & ((1u << s) - 1u), half = 1u << (s - 1);
+  if (rem < half) return {(int)fl, (int)fl};
+  if (rem > half) return {(int)fl + 1, (int)fl + 1};
+  return {(int)(fl + (fl & 1u)), (int)(fl + ((fl & 1u) ^ 1u))};  // tie: round to the even result
+}
+
+__device__ __forceinline__ void grid_of(float c, int &C, int &ue) {
+  const uint32_t bits = __float_as_uint(c);
+  const int ex = (bits >> 23) & 0xff;
+  ue = (ex ? ex : 1) - 127 - 23;
+  C = (int)((bits & 0x7fffffu) | (ex ? 0x800000u : 0u));
+}
+
+struct ScanShared {
+  IncMap warp_tot[kScanThreads / 32];
+  IncMap warp_pre[kScanThreads / 32];
+  float c;    // running sum after the processed prefix
+  int pos;    // first unprocessed chunk-local index
+  int cross;  // first chunk-local index leaving the grid model
+  int found;  // first chunk-local index with r <= cum
+  int done;
+};
+
+// Exclusive block scan of IncMap (thread order).
+__device__ __forceinline__ IncMap block_exclusive_scan(IncMap x, ScanShared &sh) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  IncMap inc = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    IncMap y;
+    y.e = __shfl_up_sync(0xffffffffu, inc.e, o);
+    y.o = __shfl_up_sync(0xffffffffu, inc.o, o);
+    if (lane >= o) inc = compose(y, inc);
+  }
+  if (lane == 31) sh.warp_tot[w] = inc;
   __syncthreads();
-  for (int64_t ch = 0; ch < nch; ++ch) {
-    if (warp != 0) {
-      if (ch + 1 < nch) fill(ch + 1);
-    } else if (lane == 0) {
-      const int64_t base = ch * kChunk;
-      const int n = (int)((V - base) < kChunk ? (V - base) : kChunk);
-      const float *src = sh.buf[ch & 1];
-      int j = 0;
-      int hit = -1;
-      for (; j + 4 <= n; j += 4) {
-        float4 v = *reinterpret_cast<const float4 *>(src + j);
-        float c0 = __fadd_rn(cum, v.x);
-        float c1 = __fadd_rn(c0, v.y);
-        float c2 = __fadd_rn(c1, v.z);
-        float c3 = __fadd_rn(c2, v.w);
-        if (r <= c0) { hit = j; break; }
-        if (r <= c1) { hit = j + 1; break; }
-        if (r <= c2) { hit = j + 2; break; }
-        if (r <= c3) { hit = j + 3; break; }
-        cum = c3;
+  if (w == 0) {
+    IncMap ti = lane < kScanThreads / 32 ? sh.warp_tot[lane] : IncMap{0, 0};
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      IncMap y;
+      y.e = __shfl_up_sync(0xffffffffu, ti.e, o);
+      y.o = __shfl_up_sync(0xffffffffu, ti.o, o);
+      if (lane >= o) ti = compose(y, ti);
+    }
+    IncMap ex;
+    ex.e = __shfl_up_sync(0xffffffffu, ti.e, 1);
+    ex.o = __shfl_up_sync(0xffffffffu, ti.o, 1);
+    if (lane == 0) ex = IncMap{0, 0};
+    if (lane < kScanThreads / 32) sh.warp_pre[lane] = ex;
+  }
+  __syncthreads();
+  IncMap lex;
+  lex.e = __shfl_up_sync(0xffffffffu, inc.e, 1);
+  lex.o = __shfl_up_sync(0xffffffffu, inc.o, 1);
+  if (lane == 0) lex = IncMap{0, 0};
+  return compose(sh.warp_pre[w], lex);
+}
+
+// Sequential fp32 accumulation of the values v_0..v_{V-1} (all >= 0 or
+// NaN/Inf) that f(i0, out[8]) produces eight at a time.
+// SEARCH == false: returns the total (the reference's `sum`).
+// SEARCH == true : *hit = the first i with r <= cum_i, or V-1.
+template <bool SEARCH, class F>
+__device__ float exact_chain(F f, int64_t V, float r, int64_t *hit, ScanShared &sh) {
+  const int tid = threadIdx.x;
+  if (tid == 0) { sh.c = 0.0f; sh.done = 0; }
+  __syncthreads();
+  int64_t result = -1;
+  for (int64_t base = 0; base < V; base += kScanChunk) {
+    const int n = (int)((V - base) < kScanChunk ? (V - base) : kScanChunk);
+    float v[kPerThread];
+#pragma unroll
+    for (int j = 0; j < kPerThread; j += 8) {
+      const int li = tid * kPerThread + j;
+      float t8[8];
+      if (li < n) f(base + li, t8);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[j + q] = (li + q < n) ? t8[q] : 0.0f;
+    }
+    if (tid == 0) sh.pos = 0;
+    __syncthreads();
+    while (true) {
+      const int pos = sh.pos;
+      const float c0 = sh.c;
+      if (pos >= n) break;
+      if (tid == 0) { sh.cross = INT_MAX; sh.found = INT_MAX; }
+      int C0, ue;
+      grid_of(c0, C0, ue);
+      IncMap loc{0, 0};
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j) {
+        const int li = tid * kPerThread + j;
+        if (li >= pos && li < n) loc = compose(loc, elem_map(v[j], ue));
       }
-      if (hit < 0) {
-        for (; j < n; ++j) {
-          cum = __fadd_rn(cum, src[j]);
-          if (r <= cum) { hit = j; break; }
+      const IncMap pre = block_exclusive_scan(loc, sh);  // its barriers order the resets above
+      int C = apply(pre, C0);
+      if (C >= kTop) C = kTop;  // a crossing lies before this thread's elements
+      int my_cross = INT_MAX, my_found = INT_MAX;
+      if (C < kTop) {
+#pragma unroll
+        for (int j = 0; j < kPerThread; ++j) {
+          const int li = tid * kPerThread + j;
+          if (li < pos || li >= n || my_cross != INT_MAX || my_found != INT_MAX) continue;
+          const int Cn = apply(elem_map(v[j], ue), C);
+          if (Cn >= kTop) { my_cross = li; continue; }
+          C = Cn;
+          if (SEARCH && r <= ldexpf((float)C, ue)) my_found = li;
         }
       }
-      if (hit >= 0) sh.found = base + hit;
+      if (my_cross != INT_MAX) atomicMin(&sh.cross, my_cross);
+      if (my_found != INT_MAX) atomicMin(&sh.found, my_found);
+      __syncthreads();
+      const int cross = sh.cross, found = sh.found;
+      if (SEARCH && found < cross) { result = base + found; break; }
+      if (cross == INT_MAX) {
+        // chunk finished: the owner of the last element publishes the sum
+        if (tid == (n - 1) / kPerThread) {
+          sh.c = ldexpf((float)C, ue);
+          sh.pos = n;
+        }
+        __syncthreads();
+        break;
+      }
+      // element `cross` leaves the grid: apply it directly in fp32
+      if (tid == cross / kPerThread) {
+        int Cp = apply(pre, C0);
+#pragma unroll
+        for (int j = 0; j < kPerThread; ++j) {
+          const int li = tid * kPerThread + j;
+          if (li >= pos && li < cross) Cp = apply(elem_map(v[j], ue), Cp);
+        }
+        const float cprev = ldexpf((float)Cp, ue);  // exact: Cp < 2^24 on the 2^ue grid
+        float vx = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kPerThread; ++j)
+          if (tid * kPerThread + j == cross) vx = v[j];
+        const float cn = __fadd_rn(cprev, vx);
+        sh.c = cn;
+        sh.pos = cross + 1;
+        sh.done = (SEARCH && r <= cn) ? 1 : (isnan(cn) || isinf(cn)) ? 2 : 0;
+        sh.found = cross;
+      }
+      __syncthreads();
+      if (sh.done == 1) { result = base + sh.found; break; }
+      if (sh.done == 2) break;  // NaN / Inf: nothing later can match, the sum is final
     }
+    if (result >= 0 || sh.done == 2) break;
     __syncthreads();
-    if (sh.found >= 0) break;
   }
-  int64_t res = sh.found >= 0 ? sh.found : V - 1;
+  const float total = sh.c;
   __syncthreads();
-  return res;
+  if (SEARCH) *hit = result >= 0 ? result : V - 1;
+  return total;
 }
 
 // First index of the largest P value in a row (std::max_element semantics).
@@ -283,7 +415,7 @@ enum Mode : int { kDone = 0, kResidual = 1, kBonus = 2 };
 template <typename T>
 __global__ void __launch_bounds__(kDecideThreads)
 decide_kernel(cf_accept_args a, float c, const RowStat *stats) {
-  __shared__ ChainShared sh;
+  __shared__ ScanShared sh;
   __shared__ int s_mode, s_row, s_na;
   __shared__ float s_r;
   const int b = blockIdx.x, tid = threadIdx.x;
@@ -363,24 +495,38 @@ decide_kernel(cf_accept_args a, float c, const RowStat *stats) {
   int64_t tok;
   const T *xt = row_ptr<T>(a.target_logits, a.target_seq_stride, a.target_row_stride, b, row);
   const RowStat stt = st[K + row];
-  auto p_of = [&](int64_t i) { return prob_of(cf::to_float(xt[i]), c, stt); };
+  auto p8 = [&](int64_t i0, float (&o)[8]) {
+    load8<T>(xt, i0, V, o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o[q] = prob_of(o[q], c, stt);
+  };
   if (mode == kResidual) {
     // speculative.cpp:26-48
     const T *xd = row_ptr<T>(a.draft_logits, a.draft_seq_stride, a.draft_row_stride, b, row);
     const RowStat std_ = st[row];
-    auto resid = [&](int64_t i) {
-      float d = __fsub_rn(p_of(i), prob_of(cf::to_float(xd[i]), c, std_));
-      return d > 0.0f ? d : 0.0f;  // std::max(0.0f, d)
+    auto resid8 = [&](int64_t i0, float (&o)[8]) {
+      float d8[8];
+      load8<T>(xt, i0, V, o);
+      load8<T>(xd, i0, V, d8);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float d = __fsub_rn(prob_of(o[q], c, stt), prob_of(d8[q], c, std_));
+        o[q] = d > 0.0f ? d : 0.0f;  // std::max(0.0f, d)
+      }
     };
-    const float sum = serial_sum(resid, V, sh);
+    const float sum = exact_chain<false>(resid8, V, r, nullptr, sh);
     if (sum <= 1e-6f) {
-      tok = serial_search(p_of, V, r, sh);
+      exact_chain<true>(p8, V, r, &tok, sh);
     } else {
-      auto normed = [&](int64_t i) { return __fdiv_rn(resid(i), sum); };
-      tok = serial_search(normed, V, r, sh);
+      auto normed8 = [&](int64_t i0, float (&o)[8]) {
+        resid8(i0, o);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o[q] = __fdiv_rn(o[q], sum);
+      };
+      exact_chain<true>(normed8, V, r, &tok, sh);
     }
   } else {
-    tok = serial_search(p_of, V, r, sh);  // bonus, speculative.cpp:97
+    exact_chain<true>(p8, V, r, &tok, sh);  // bonus, speculative.cpp:97
   }
   if (tid == 0) {
     out[s_na] = (int32_t)tok;
