@@ -22,6 +22,7 @@
 #include "common.cuh"
 
 #include <limits.h>
+#include <mutex>
 #include <math.h>
 
 namespace {
@@ -573,3 +574,50 @@ extern "C" int cf_accept_sample(const cf_accept_args *args, void *stream) {
     default: return CF_EINVAL;
   }
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot allocate device memory at
+// all: code running where cudaMalloc is off limits (an allocator hook, a
+// host runtime that owns every byte of device memory, a plugin that may only
+// touch the buffers it is handed).  For them the per-row softmax statistics
+// live in a fixed array inside this library instead of a caller workspace.
+// The array is kAcceptScratchRows RowStats (512 KiB) on every GPU that loads
+// the library, held until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kAcceptScratchRows = 65536;  // batch * (2k + 1) must not exceed this
+static __device__ __align__(256) RowStat g_accept_scratch[kAcceptScratchRows];
+
+constexpr int kMaxDevices = 64;
+void *g_scratch_ptr[kMaxDevices];
+std::mutex g_scratch_mu;
+
+// Device address of g_accept_scratch on the current device (looked up once
+// per device; the host-side symbol itself is not a device address).
+int scratch_ptr(void **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CF_ECUDA;
+  std::lock_guard<std::mutex> g(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_accept_scratch) != cudaSuccess || !p) return CF_ECUDA;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return CF_OK;
+}
+}  // namespace
+
+extern "C" int cf_accept_sample_noalloc(const cf_accept_args *args, void *stream) {
+  if (!args) return CF_EINVAL;
+  if (args->batch < 0 || args->k < 0) return CF_EINVAL;
+  if ((int64_t)args->batch * (2 * (int64_t)args->k + 1) > kAcceptScratchRows) return CF_ERANGE;
+  void *ws = nullptr;
+  const int rc = scratch_ptr(&ws);
+  if (rc != CF_OK) return rc;
+  cf_accept_args a = *args;
+  a.workspace = ws;  // every row statistic is written before it is read: nothing to clear
+  return cf_accept_sample(&a, stream);
+}
+
+extern "C" int cf_accept_noalloc_max_rows(void) { return kAcceptScratchRows; }

@@ -113,6 +113,20 @@ typedef struct cf_accept_args {
 size_t cf_accept_workspace_bytes(int32_t batch, int32_t k);
 int cf_accept_sample(const cf_accept_args *args, void *stream);
 
+/* Same as cf_accept_sample, for callers that must not allocate device memory
+ * (an allocator hook, a runtime that owns all device memory, a plugin limited
+ * to the buffers it is given).  No counterpart in the reference.  args->workspace
+ * is ignored: the row statistics go to a fixed array compiled into this
+ * library (cf_accept_noalloc_max_rows() rows, 512 KiB per GPU that loads the
+ * library, held until exit).  batch * (2k + 1) beyond that limit returns
+ * CF_ERANGE and launches nothing.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  All calls share the array: calls that can run
+ * at the same time on the GPU (different streams, different host threads)
+ * race and must be serialised by the caller.  No cudaMalloc / cudaFree. */
+int cf_accept_sample_noalloc(const cf_accept_args *args, void *stream);
+int cf_accept_noalloc_max_rows(void);
+
 /* ------------------------------------------------------------------------
  * GEMM on tcgen05 tensor cores (TMEM accumulators, TMA-staged operands)
  *
