@@ -41,6 +41,7 @@ class CfGemmArgs(ctypes.Structure):
         ("x", _P), ("ldx", _I64), ("w", _P), ("scales", _P), ("y", _P), ("ldy", _I64),
         ("residual", _P), ("ldr", _I64), ("split_k", _I32), ("workspace", _P),
         ("workspace_bytes", ctypes.c_size_t), ("status", _P), ("timeout_ns", ctypes.c_uint64),
+        ("trace", _P),
     ]
 
 

@@ -11,17 +11,23 @@
 // (signed INT4, the `zeros == 8` case of int4_gemm_dequant.cu:87-92).
 //
 // Design (swap-AB, because M = tokens is small and N*K = weights is large):
-//   the MMA computes D^T[n, m] = W[n, :] . X[m, :]; the weight tile
-//   (128 n x 64 k) is the tcgen05 "A" operand and the token tile (up to 512
-//   tokens x 64 k, in <= 256-token MMA chunks) the "B" operand, so every
-//   dequantised weight element feeds up to 512 tokens.  One CTA = one
-//   128-row weight tile x one K split x one token slice; 6 warps:
-//     warp 0      TMA producer (packed weights, group scales, token tile)
-//     warp 1      TMEM allocator + the single MMA-issuing thread
-//     warps 2-5   INT4 -> bf16 dequantisation into the 128-B swizzled A tile,
-//                 then the epilogue (tcgen05.ld from TMEM -> global)
-//   Every mbarrier wait is bounded (a device status word records CF_ETIMEOUT).
-//   No TMA multicast is used.
+//   the MMA computes D^T[n, m] = W[n, :] . X[m, :]; weight rows are the
+//   tcgen05 "A" operand (M = 128 per MMA) and the token tile (<= 256 tokens
+//   x 64 k) the "B" operand.  One CTA = 256 weight rows (two 128-row MMA
+//   halves, two TMEM accumulators) x one K split x one token slice, so each
+//   token tile the SM pulls through its TMA path feeds 256 weight rows: the
+//   per-SM TMA path (~100 GB/s from L2, ~0.1-0.3 us per op from one issuing
+//   thread, measured) is what the tile shape is sized against.  7 warps:
+//     warp 0      weight producer (lane 0 packed W, lane 1 group scales)
+//     warp 1      TMEM allocator + MMA issue (whole warp, elect.sync lane)
+//     warps 2-9   INT4 -> bf16 dequantisation into the 128-B swizzled A
+//                 tiles (one weight row per thread), then the epilogue
+//                 (tcgen05.ld -> shared staging -> 16-byte row-contiguous
+//                 stores)
+//     warp 10     token-tile producer
+//   Three independent rings (packed W, dequantised A, token tile), every
+//   mbarrier wait bounded (a device status word records CF_ETIMEOUT), no TMA
+//   multicast.
 //
 // The packed weights are consumed in a kernel-native nibble order produced
 // once per weight by cf_w4a16_repack (the same values; see dequant8()).
@@ -30,28 +36,35 @@
 #include "tmap.h"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace {
 
 using namespace cf::sm100;
 
-constexpr int kThreads = 192;
-constexpr int BN = 128;  // weight rows per CTA (MMA M)
-constexpr int BK = 64;   // k per pipeline stage: one 128-B swizzle atom of 16-bit elements
-constexpr int kMaxSlice = 512;
+constexpr int kThreads = 352;  // 11 warps
+constexpr int HN = 128;        // weight rows per MMA (tcgen05 M)
+constexpr int TN = 256;        // weight rows per CTA (two MMA halves)
+constexpr int BK = 64;         // k per pipeline stage: one 128-B swizzle atom of 16-bit elements
+constexpr int kMaxSlice = 256; // tokens per CTA (MMA N), two accumulators fit 512 TMEM columns
 constexpr int kMaxSmem = 232448;
-constexpr uint32_t kATileBytes = BN * BK * 2;  // 16 KB
-constexpr uint32_t kWPackBytes = (BK / 8) * BN * 4;  // 4 KB
-constexpr uint32_t kScaleBytes = BN * 2;
+constexpr uint32_t kHalfBytes = HN * BK * 2;           // 16 KB dequantised half tile
+constexpr uint32_t kAStageBytes = 2 * kHalfBytes;      // 32 KB
+constexpr uint32_t kWPackBytes = (BK / 8) * TN * 4;    // 8 KB packed INT4
+constexpr uint32_t kScaleBytes = TN * 2;               // 512 B fp16 group scales
+constexpr uint32_t kWStageBytes = kWPackBytes + kScaleBytes;
 constexpr uint64_t kDrainNs = 1000000000ull;
 
 enum WMode : int { kInt4 = 0, kDense = 1 };
 
 struct GemmParams {
   int M, N, K;
-  int m_slice, chunks, chunk_rows, stages, kb_per_split, splits;
-  uint32_t stage_bytes, off_x, off_w, off_s;
+  int m_slice, kb_per_split, splits;
+  int sa, sx, sw;                  // ring depths: dequantised A, token tile X, packed W (+scales)
+  uint32_t off_x, off_w, off_bar;  // ring bases (A ring at 0)
+  uint32_t x_bytes;
   uint32_t tmem_cols, idesc;
+  uint32_t a_tcol;                 // INT4: first TMEM column of the dequantised-A stages
   void *y;
   int64_t ldy;
   const void *residual;
@@ -59,6 +72,8 @@ struct GemmParams {
   float *partial;
   int *status;
   uint64_t timeout_ns;
+  unsigned long long *trace;
+  int dbg_nox;
 };
 
 // 8 repacked nibbles -> 8 bf16 (k order 0..7).  Repacked nibble position p
@@ -92,28 +107,40 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
             const __grid_constant__ CUtensorMap tm_s, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int S = p.stages;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * p.stage_bytes);
-  uint64_t *deq = full + S;
-  uint64_t *empty = deq + S;
-  uint64_t *accf = empty + S;
+  const int SA = p.sa, SX = p.sx, SW = p.sw;
+  uint8_t *a_ring = smem;                 // SA x 32 KB weight tiles (two 128-row halves)
+  uint8_t *x_ring = smem + p.off_x;       // SX x x_bytes token tiles
+  uint8_t *w_ring = smem + p.off_w;       // SW x (8 KB packed + 512 B scales), INT4 only
+  uint64_t *wfull = reinterpret_cast<uint64_t *>(smem + p.off_bar);
+  uint64_t *wempty = wfull + SW;
+  uint64_t *xfull = wempty + SW;
+  uint64_t *xempty = xfull + SX;
+  uint64_t *afull = xempty + SX;
+  uint64_t *aempty = afull + SA;
+  uint64_t *accf = aempty + SA;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int split = blockIdx.y;
-  const int m0 = blockIdx.z * p.m_slice;
+  const int m0 = blockIdx.x * p.m_slice;
+  const int n0 = blockIdx.y * TN;
+  const int split = blockIdx.z;
+  const int halves = (n0 + HN < p.N) ? 2 : 1;
   const int mrows = min(p.m_slice, p.M - m0);
   const int kbs = p.K / BK;
   const int kb0 = split * p.kb_per_split;
   const int nkb = min(p.kb_per_split, kbs - kb0);
+  // Rotated k order: CTAs start at different k-blocks so they do not all read the
+  // same token-tile lines of L2 at the same moment (each CTA's order is fixed).
+  const int rot = nkb > 0 ? (int)((blockIdx.y * 7u + blockIdx.x * 3u) % (unsigned)nkb) : 0;
+  auto kb_of = [&](int i) { int j = i + rot; return kb0 + (j >= nkb ? j - nkb : j); };
+  const bool tr = p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+#define CF_TRACE(role, i) \
+  if (tr && (i) < 512) p.trace[(role) * 512 + (i)] = clock64()
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&deq[s], 4);
-      mbar_init(&empty[s], 1);
-    }
+    for (int s = 0; s < SW; ++s) { mbar_init(&wfull[s], 1); mbar_init(&wempty[s], 8); }
+    for (int s = 0; s < SX; ++s) { mbar_init(&xfull[s], 1); mbar_init(&xempty[s], 1); }
+    for (int s = 0; s < SA; ++s) { mbar_init(&afull[s], WM == kInt4 ? 8 : 1); mbar_init(&aempty[s], 1); }
     mbar_init(accf, 1);
     fence_mbar_init();
   }
@@ -130,116 +157,200 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   bool ok = true;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      const uint32_t x_bytes = (uint32_t)(p.chunks * p.chunk_rows) * 128u;
-      const uint32_t bytes = x_bytes + (WM == kInt4 ? kWPackBytes + kScaleBytes : kATileBytes);
-      int issued = 0;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (uint32_t)(i / S) & 1u;
-        if (i >= S && !mbar_wait(&empty[s], ph ^ 1u, p.timeout_ns)) { ok = false; break; }
-        uint8_t *st = smem + s * p.stage_bytes;
-        const int kb = kb0 + i;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        for (int j = 0; j < p.chunks; ++j)
-          tma_load_2d(st + p.off_x + j * p.chunk_rows * 128, &tm_x, &full[s], kb * BK, m0 + j * p.chunk_rows);
-        if (WM == kInt4) {
-          tma_load_2d(st + p.off_w, &tm_w, &full[s], n0, kb * (BK / 8));
-          tma_load_2d(st + p.off_s, &tm_s, &full[s], n0, (kb * BK) / 128);
-        } else {
-          tma_load_2d(st, &tm_w, &full[s], kb * BK, n0);
-        }
-        issued = i + 1;
+    // ---------------- weight producer ----------------
+    const int S = WM == kInt4 ? SW : SA;
+    uint64_t *fullb = WM == kInt4 ? wfull : afull;
+    uint64_t *emptyb = WM == kInt4 ? wempty : aempty;
+    int issued = 0;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % S;
+      const uint32_t ph = (uint32_t)(i / S) & 1u;
+      if (i >= S && !mbar_wait_warp(&emptyb[s], ph ^ 1u, p.timeout_ns)) { ok = false; break; }
+      const int kb = kb_of(i);
+      if (lane == 0) {
+        CF_TRACE(0, i);
+        mbar_arrive_expect_tx(&fullb[s], WM == kInt4 ? kWStageBytes : (uint32_t)halves * kHalfBytes);
       }
-      if (!ok) {  // let our own copies land before the CTA can exit
-        for (int j = max(0, issued - S); j < issued; ++j)
-          mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u, kDrainNs);
+      __syncwarp();
+      // The issuing lane rotates with the stage: one thread's TMA copies were measured
+      // not to overlap one another, copies from different threads do.
+      const int l0 = (2 * i) & 31;
+      if (WM == kInt4) {
+        uint8_t *st = w_ring + s * kWStageBytes;
+        if (lane == l0) tma_load_2d(st, &tm_w, &fullb[s], n0, kb * (BK / 8));
+        if (lane == l0 + 1) tma_load_2d(st + kWPackBytes, &tm_s, &fullb[s], n0, (kb * BK) / 128);
+      } else {
+        if (lane >= l0 && lane < l0 + halves)
+          tma_load_2d(a_ring + s * kAStageBytes + (lane - l0) * kHalfBytes, &tm_w, &fullb[s], kb * BK,
+                      n0 + (lane - l0) * HN);
       }
+      __syncwarp();
+      issued = i + 1;
     }
+    if (!ok)  // let our own copies land before the CTA can exit
+      for (int j = max(0, issued - S); j < issued; ++j)
+        mbar_wait_warp(&fullb[j % S], (uint32_t)(j / S) & 1u, kDrainNs);
+  } else if (warp == 10) {
+    // ---------------- token-tile producer ----------------
+    int issued = 0;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % SX;
+      const uint32_t ph = (uint32_t)(i / SX) & 1u;
+      if (i >= SX && !mbar_wait_warp(&xempty[s], ph ^ 1u, p.timeout_ns)) { ok = false; break; }
+      const int kb = kb_of(i);
+      // one 16-row box (2 KB, 1024-B aligned) per lane: a single issuing thread
+      // sustains only ~30 GB/s of TMA traffic, many lanes in parallel far more
+      if (lane == 0) {
+        CF_TRACE(4, i);
+        mbar_arrive_expect_tx(&xfull[s], (p.dbg_nox & 1) ? 0 : p.x_bytes);
+      }
+      __syncwarp();
+      {
+        const int nbox = p.m_slice / 16;
+        const int b = (lane - i * nbox) & 31;  // box handled by this lane (rotating per stage)
+        if (!(p.dbg_nox & 1) && b < nbox)
+          tma_load_2d(x_ring + s * p.x_bytes + b * 2048, &tm_x, &xfull[s], kb * BK, m0 + b * 16);
+      }
+      __syncwarp();
+      issued = i + 1;
+    }
+    if (!ok)
+      for (int j = max(0, issued - SX); j < issued; ++j)
+        mbar_wait_warp(&xfull[j % SX], (uint32_t)(j / SX) & 1u, kDrainNs);
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- single MMA-issuing thread ----------------
-      const uint32_t idesc = p.idesc;
-      int i = 0;
-      for (; i < nkb; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (uint32_t)(i / S) & 1u;
-        if (!mbar_wait(&full[s], ph, p.timeout_ns)) { ok = false; break; }
-        if (WM == kInt4 && !mbar_wait(&deq[s], ph, p.timeout_ns)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + s * p.stage_bytes);
-        const uint32_t x_base = a_base + p.off_x;
-#pragma unroll
+    // ---------------- MMA issue: the whole warp walks the loop, one elected lane issues ----------------
+    const uint32_t idesc = p.idesc;
+    for (int i = 0; i < nkb; ++i) {
+      const int sa = i % SA, sx = i % SX;
+      if (lane == 0) CF_TRACE(6, i);
+      if (!mbar_wait_warp(&afull[sa], (uint32_t)(i / SA) & 1u, p.timeout_ns)) { ok = false; break; }
+      if (lane == 0) CF_TRACE(7, i);
+      if (!mbar_wait_warp(&xfull[sx], (uint32_t)(i / SX) & 1u, p.timeout_ns)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t a_base = smem_u32(a_ring + sa * kAStageBytes);
+      const uint32_t x_base = smem_u32(x_ring + sx * p.x_bytes);
+      if (elect_one()) {
+        CF_TRACE(3, i);
+        if (!(p.dbg_nox & 8))
         for (int k16 = 0; k16 < BK / 16; ++k16) {
-          const uint64_t ad = desc_kmajor_sw128(a_base + k16 * 32);
-          for (int j = 0; j < p.chunks; ++j) {
-            const uint64_t bd = desc_kmajor_sw128(x_base + j * p.chunk_rows * 128 + k16 * 32);
-            mma_f16(tmem + (uint32_t)(j * p.chunk_rows), ad, bd, idesc, (i > 0 || k16 > 0) ? 1u : 0u);
+          const uint64_t bd = desc_kmajor_sw128(x_base + k16 * 32);
+          for (int h = 0; h < halves; ++h) {
+            const uint32_t acc = (i > 0 || k16 > 0) ? 1u : 0u;
+            if (WM == kInt4) {  // A from TMEM: 32 columns per half per stage, 8 per k16
+              const uint32_t at = tmem + p.a_tcol + (uint32_t)((sa * 2 + h) * 32 + k16 * 8);
+              mma_f16_ts(tmem + (uint32_t)(h * p.m_slice), at, bd, idesc, acc);
+            } else {
+              const uint64_t ad = desc_kmajor_sw128(a_base + h * kHalfBytes + k16 * 32);
+              mma_f16(tmem + (uint32_t)(h * p.m_slice), ad, bd, idesc, acc);
+            }
           }
         }
-        mma_commit(&empty[s]);
+        mma_commit(&aempty[sa]);
+        mma_commit(&xempty[sx]);
+        CF_TRACE(8, i);
       }
-      mma_commit(accf);  // completes when every issued MMA has finished
+      __syncwarp();
     }
+    if (elect_one()) mma_commit(accf);  // completes when every issued MMA has finished
+    __syncwarp();
   } else {
-    // ---------------- dequantisation (warps 2-5) ----------------
-    const int t = threadIdx.x - 64;  // weight row within the tile
+    // ---------------- dequantisation (warps 2-9) straight into TMEM ----------------
+    // Warp w may only touch TMEM lanes 32*(w%4)..+31, so warp w owns rows
+    // (w%4)*32 + lane of half h = (w-2)/4; each thread dequantises its row's
+    // 64 k values and stores them with one tcgen05.st (32 columns).
+    const int q = warp & 3, h = (warp - 2) >> 2;
+    const int row = q * 32 + lane;  // within the half == TMEM lane
+    const int t = h * HN + row;     // within the 256-row tile
     if (WM == kInt4) {
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (uint32_t)(i / S) & 1u;
-        if (!mbar_wait(&full[s], ph, p.timeout_ns)) { ok = false; break; }
-        uint8_t *st = smem + s * p.stage_bytes;
-        const uint32_t *wp = reinterpret_cast<const uint32_t *>(st + p.off_w);
-        const __half sc = reinterpret_cast<const __half *>(st + p.off_s)[t];
-        const __nv_bfloat16 sb = __float2bfloat16_rn(__half2float(sc));
+        const int sw = i % SW, sa = i % SA;
+        if (!mbar_wait(&wfull[sw], (uint32_t)(i / SW) & 1u, p.timeout_ns)) { ok = false; break; }
+        if (i >= SA && !mbar_wait(&aempty[sa], ((uint32_t)(i / SA) & 1u) ^ 1u, p.timeout_ns)) { ok = false; break; }
+        tc_fence_after();
+        if (threadIdx.x == 64) CF_TRACE(1, i);
+        const uint8_t *st = w_ring + sw * kWStageBytes;
+        const uint32_t *wp = reinterpret_cast<const uint32_t *>(st);
+        const __nv_bfloat16 sb =
+            __float2bfloat16_rn(__half2float(reinterpret_cast<const __half *>(st + kWPackBytes)[t]));
         const __nv_bfloat162 s2 = __halves2bfloat162(sb, sb);
-        uint8_t *arow = st + t * 128;
         uint32_t w[8];
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) w[kk] = wp[kk * BN + t];
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          *reinterpret_cast<uint4 *>(arow + ((kk ^ (t & 7)) << 4)) = dequant8(w[kk], s2);
-        fence_proxy_async_smem();
+        for (int kk = 0; kk < 8; ++kk) w[kk] = wp[kk * TN + t];
         __syncwarp();
-        if (lane == 0) mbar_arrive(&deq[s]);
+        if (lane == 0) mbar_arrive(&wempty[sw]);  // packed words are in registers
+        uint32_t a[32];
+        if (!(p.dbg_nox & 4)) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint4 v = dequant8(w[kk], s2);
+            a[4 * kk + 0] = v.x; a[4 * kk + 1] = v.y; a[4 * kk + 2] = v.z; a[4 * kk + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < 32; ++kk) a[kk] = w[kk & 7];
+        }
+        if (h < halves && !(p.dbg_nox & 2))
+          tmem_st_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + p.a_tcol + (uint32_t)((sa * 2 + h) * 32), a);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[sa]);
+        if (threadIdx.x == 64) CF_TRACE(2, i);
       }
     }
     // ---------------- epilogue ----------------
     if (!mbar_wait(accf, 0, ok ? p.timeout_ns : kDrainNs)) ok = false;
     tc_fence_after();
+    if (threadIdx.x == 64) CF_TRACE(5, 0);
     if (ok) {
-      const int q = warp & 3;  // TMEM lane quarter this warp may access
-      const int n = n0 + q * 32 + lane;
+      // TMEM row (this lane) x 32 token columns -> a per-warp staging tile in the (now idle)
+      // A ring, then 16-byte row-contiguous stores: each token row's 32 outputs are 64 B
+      // (bf16) or 128 B (fp32 partials) of one global row.
+      float *stg = reinterpret_cast<float *>(a_ring + (warp - 2) * 4096);  // [32 tokens][32 n]
       T *y = reinterpret_cast<T *>(p.y);
       const T *res = reinterpret_cast<const T *>(p.residual);
-      for (int c = 0; c < mrows; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
-        tmem_ld_wait();
-        const int lim = min(32, mrows - c);
-        if (p.splits > 1) {
-          float *dst = p.partial + ((int64_t)split * p.M + (m0 + c)) * p.N + n;
+      if (h < halves) {  // warps 2-5 drain half 0, warps 6-9 half 1
+        const int nw = n0 + h * HN + q * 32;
+        for (int c = 0; c < mrows; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * p.m_slice + c), r);
+          tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < lim) dst[(int64_t)j * p.N] = __uint_as_float(r[j]);
-        } else {
+          for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = __uint_as_float(r[j]);
+          __syncwarp();
+          const int lim = min(32, mrows - c);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+          for (int pass = 0; pass < 8; ++pass) {
+            const int j = pass * 4 + (lane >> 3);  // token within the 32
+            const int nn = (lane & 7) * 4;         // 4 consecutive outputs
             if (j < lim) {
+              const float4 v = *reinterpret_cast<const float4 *>(stg + j * 32 + nn);
               const int64_t m = m0 + c + j;
-              float v = __uint_as_float(r[j]);
-              if (res) v += cf::to_float(res[m * p.ldr + n]);
-              y[m * p.ldy + n] = from_f<T>(v);
+              if (p.splits > 1) {
+                *reinterpret_cast<float4 *>(p.partial + ((int64_t)split * p.M + m) * p.N + nw + nn) = v;
+              } else {
+                float o[4] = {v.x, v.y, v.z, v.w};
+                if (res) {
+                  const uint2 rr = *reinterpret_cast<const uint2 *>(res + m * p.ldr + nw + nn);
+                  const T *rp = reinterpret_cast<const T *>(&rr);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) o[e] += cf::to_float(rp[e]);
+                }
+                uint2 w;
+                T *wp = reinterpret_cast<T *>(&w);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) wp[e] = from_f<T>(o[e]);
+                *reinterpret_cast<uint2 *>(y + m * p.ldy + nw + nn) = w;
+              }
             }
           }
+          __syncwarp();
         }
       }
     }
   }
   if (!ok && p.status) atomicExch(p.status, CF_ETIMEOUT);
+  if (threadIdx.x == 64) CF_TRACE(5, 1);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -287,8 +398,8 @@ __global__ void repack_kernel(const uint32_t *src, uint32_t *dst, int64_t n_word
 }
 
 struct Plan {
-  int slices, m_slice, chunks, chunk_rows, stages, splits, kb_per_split;
-  uint32_t stage_bytes, off_x, off_w, off_s, tmem_cols;
+  int slices, m_slice, splits, kb_per_split, sa, sx, sw, ntiles;
+  uint32_t x_bytes, off_x, off_w, off_bar, tmem_cols, a_tcol;
   size_t smem;
 };
 
@@ -303,25 +414,43 @@ int num_sms() {
 }
 
 bool make_plan(int M, int N, int K, int split_req, bool int4, Plan &pl) {
-  pl.slices = (M + kMaxSlice - 1) / kMaxSlice;
+  // INT4: TMEM = two accumulators (2 x m_slice columns) + >= 2 dequantised-A stages (64 columns each)
+  auto env0 = [](const char *n, int d) { const char *v = getenv(n); return v ? atoi(v) : d; };
+  const int max_slice = int4 ? env0("CF_GEMM_MAXSLICE", 192) : kMaxSlice;
+  pl.slices = (M + max_slice - 1) / max_slice;
   const int per = (M + pl.slices - 1) / pl.slices;
-  pl.chunks = (per + 255) / 256;
-  pl.chunk_rows = ((per + pl.chunks - 1) / pl.chunks + 15) / 16 * 16;
-  pl.m_slice = pl.chunks * pl.chunk_rows;
-  if (pl.m_slice > kMaxSlice) return false;
-  pl.off_x = kATileBytes;
-  pl.off_w = pl.off_x + (uint32_t)pl.m_slice * 128u;
-  pl.off_s = pl.off_w + (int4 ? kWPackBytes : 0);
-  pl.stage_bytes = (pl.off_s + (int4 ? kScaleBytes : 0) + 1023u) & ~1023u;
-  const size_t fixed = 1024 + 1024;  // alignment slack + barriers
-  pl.stages = (int)std::min<size_t>(6, (kMaxSmem - fixed) / pl.stage_bytes);
-  if (pl.stages < 2) return false;
-  pl.smem = fixed + (size_t)pl.stages * pl.stage_bytes;
-  uint32_t cols = 32;
-  while (cols < (uint32_t)pl.m_slice) cols <<= 1;
-  pl.tmem_cols = cols;
+  pl.m_slice = (per + 15) / 16 * 16;  // loaded as m_slice/16 boxes of 16 rows
+  if (pl.m_slice > max_slice) return false;
+  // smem: A ring (dense: 32 KB / stage; INT4: 32 KB epilogue staging) | X ring | W ring (8.5 KB / stage)
+  pl.x_bytes = (uint32_t)pl.m_slice * 128u;
+  const size_t budget = kMaxSmem - 1024 - 1024;  // alignment slack + barriers
+  const size_t w_stage = int4 ? kWStageBytes : 0;
+  auto env = [](const char *n, int d) { const char *v = getenv(n); return v ? atoi(v) : d; };
+  if (int4) {
+    pl.a_tcol = (2u * pl.m_slice + 31u) & ~31u;
+    pl.sa = std::min(env("CF_GEMM_SA", 4), (int)((512u - pl.a_tcol) / 64u));
+    pl.tmem_cols = 512;
+  } else {
+    pl.a_tcol = 0;
+    pl.sa = env("CF_GEMM_SA", 3);
+  }
+  const size_t a_bytes = int4 ? (size_t)kAStageBytes : pl.sa * (size_t)kAStageBytes;
+  pl.sw = int4 ? env("CF_GEMM_SW", 8) : 1;
+  pl.sx = (int)std::min<size_t>(env("CF_GEMM_SX", 6), (budget - a_bytes - pl.sw * w_stage) / pl.x_bytes);
+  if (pl.sx < 2 && !int4) { pl.sa = 2; pl.sx = (int)std::min<size_t>(4, (budget - 2 * (size_t)kAStageBytes) / pl.x_bytes); }
+  if (pl.sx < 2 || pl.sa < 2 || (int4 && pl.sw < 2)) return false;
+  pl.off_x = (uint32_t)(int4 ? kAStageBytes : pl.sa * kAStageBytes);
+  pl.off_w = pl.off_x + pl.sx * pl.x_bytes;
+  pl.off_bar = (pl.off_w + (int4 ? pl.sw * kWStageBytes : 0) + 15u) & ~15u;
+  pl.smem = 1024 + pl.off_bar + 8 * (2 * pl.sw + 2 * pl.sx + 2 * pl.sa + 1) + 16;
+  if (!int4) {
+    uint32_t cols = 32;
+    while (cols < 2u * (uint32_t)pl.m_slice) cols <<= 1;
+    pl.tmem_cols = cols;
+  }
   const int kbs = K / BK;
-  const int tiles = (N / BN) * pl.slices;
+  pl.ntiles = (N + TN - 1) / TN;
+  const int tiles = pl.ntiles * pl.slices;
   int splits = split_req > 0 ? split_req : std::max(1, num_sms() / tiles);
   splits = std::max(1, std::min(splits, kbs / 2 > 0 ? kbs / 2 : 1));
   pl.kb_per_split = (kbs + splits - 1) / splits;
@@ -334,9 +463,13 @@ int run_gemm(const cf_gemm_args &a, cudaStream_t stream) {
   const bool int4 = WM == kInt4;
   if (a.m < 0 || a.n <= 0 || a.k <= 0) return CF_EINVAL;
   if (a.m == 0) return CF_OK;
-  if (a.n % BN != 0 || a.k % (int4 ? 128 : BK) != 0) return CF_EINVAL;
+  if (a.n % HN != 0 || a.k % (int4 ? 128 : BK) != 0) return CF_EINVAL;
   if (!a.x || !a.w || !a.y || (int4 && !a.scales)) return CF_EINVAL;
   if (a.ldx < a.k || a.ldy < a.n || (a.residual && a.ldr < a.n)) return CF_EINVAL;
+  // the epilogue writes 4 outputs (8 B) per vector store
+  if (a.ldy % 4 || (a.residual && a.ldr % 4) || (reinterpret_cast<uintptr_t>(a.y) & 7) ||
+      (reinterpret_cast<uintptr_t>(a.residual) & 7))
+    return CF_EINVAL;
   Plan pl;
   if (!make_plan(a.m, a.n, a.k, a.split_k, int4, pl)) return CF_EUNSUPPORTED;
   if (pl.splits > 1) {
@@ -348,37 +481,41 @@ int run_gemm(const cf_gemm_args &a, cudaStream_t stream) {
   const CUtensorMapDataType tdt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tx, tw, ts;
-  if (!cf::make_tmap_2d(&tx, tdt, a.x, (uint64_t)a.k, (uint64_t)a.m, (uint64_t)a.ldx * 2, BK, pl.chunk_rows,
+  if (!cf::make_tmap_2d(&tx, tdt, a.x, (uint64_t)a.k, (uint64_t)a.m, (uint64_t)a.ldx * 2, BK, 16,
                         CU_TENSOR_MAP_SWIZZLE_128B))
     return CF_EINVAL;
   if (int4) {
     if (!cf::make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, (uint64_t)a.n, (uint64_t)a.k / 8,
-                          (uint64_t)a.n * 4, BN, BK / 8, CU_TENSOR_MAP_SWIZZLE_NONE))
+                          (uint64_t)a.n * 4, TN, BK / 8, CU_TENSOR_MAP_SWIZZLE_NONE))
       return CF_EINVAL;
     if (!cf::make_tmap_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.scales, (uint64_t)a.n, (uint64_t)a.k / 128,
-                          (uint64_t)a.n * 2, BN, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+                          (uint64_t)a.n * 2, TN, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
       return CF_EINVAL;
   } else {
-    if (!cf::make_tmap_2d(&tw, tdt, a.w, (uint64_t)a.k, (uint64_t)a.n, (uint64_t)a.k * 2, BK, BN,
+    if (!cf::make_tmap_2d(&tw, tdt, a.w, (uint64_t)a.k, (uint64_t)a.n, (uint64_t)a.k * 2, BK, HN,
                           CU_TENSOR_MAP_SWIZZLE_128B))
       return CF_EINVAL;
     ts = tw;
   }
   GemmParams p;
   p.M = a.m; p.N = a.n; p.K = a.k;
-  p.m_slice = pl.m_slice; p.chunks = pl.chunks; p.chunk_rows = pl.chunk_rows; p.stages = pl.stages;
+  p.m_slice = pl.m_slice;
   p.kb_per_split = pl.kb_per_split; p.splits = pl.splits;
-  p.stage_bytes = pl.stage_bytes; p.off_x = pl.off_x; p.off_w = pl.off_w; p.off_s = pl.off_s;
+  p.sa = pl.sa; p.sx = pl.sx; p.sw = pl.sw;
+  p.off_x = pl.off_x; p.off_w = pl.off_w; p.off_bar = pl.off_bar; p.x_bytes = pl.x_bytes;
   p.tmem_cols = pl.tmem_cols;
-  p.idesc = cf::sm100::idesc_bf16_f32(BN, pl.chunk_rows);
+  p.a_tcol = pl.a_tcol;
+  p.dbg_nox = getenv("CF_GEMM_DBG") ? atoi(getenv("CF_GEMM_DBG")) : 0;
+  p.idesc = cf::sm100::idesc_bf16_f32(HN, pl.m_slice);
   if (std::is_same<T, __half>::value) p.idesc &= ~((7u << 7) | (7u << 10));  // A, B format f16
   p.y = a.y; p.ldy = a.ldy; p.residual = a.residual; p.ldr = a.ldr;
   p.partial = reinterpret_cast<float *>(a.workspace);
   p.status = a.status;
   p.timeout_ns = a.timeout_ns ? a.timeout_ns : 2000000000ull;
+  p.trace = reinterpret_cast<unsigned long long *>(a.trace);
   auto kern = gemm_kernel<T, WM>;
   CF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
-  dim3 grid(a.n / BN, pl.splits, pl.slices);
+  dim3 grid(pl.slices, pl.ntiles, pl.splits);
   kern<<<grid, kThreads, pl.smem, stream>>>(tx, tw, ts, p);
   if (cudaGetLastError() != cudaSuccess) return CF_ECUDA;
   if (pl.splits > 1) {

@@ -62,7 +62,8 @@ class _Ws:
         return b
 
 
-def _gemm(fn, x, w, scales, n, residual, out, split_k, workspace, status, int4, timeout_ns=0, stream=None):
+def _gemm(fn, x, w, scales, n, residual, out, split_k, workspace, status, int4, timeout_ns=0, stream=None,
+          trace=None):
     if x.dim() != 2 or x.stride(1) != 1:
         raise ValueError("x must be 2-D with unit inner stride")
     M, K = x.shape
@@ -79,7 +80,7 @@ def _gemm(fn, x, w, scales, n, residual, out, split_k, workspace, status, int4, 
                         ldr=residual.stride(0) if residual is not None else 0,
                         split_k=split_k, workspace=workspace.data_ptr() if need else None,
                         workspace_bytes=need, status=status.data_ptr() if status is not None else None,
-                        timeout_ns=timeout_ns)
+                        timeout_ns=timeout_ns, trace=trace.data_ptr() if trace is not None else None)
     s = stream or torch.cuda.current_stream(x.device)
     _lib.check(fn(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), fn.__name__)
     _lib.count(2 if need else 1)
@@ -87,11 +88,12 @@ def _gemm(fn, x, w, scales, n, residual, out, split_k, workspace, status, int4, 
 
 
 def w4a16_gemm(x: torch.Tensor, wq_kernel: torch.Tensor, scales: torch.Tensor, *, residual=None, out=None,
-               split_k: int = 0, workspace=None, status=None, timeout_ns: int = 0, stream=None) -> torch.Tensor:
+               split_k: int = 0, workspace=None, status=None, timeout_ns: int = 0, stream=None,
+               trace=None) -> torch.Tensor:
     """y = x @ deq(W) (+ residual); x bf16 [M, K], wq_kernel from repack_int4, scales fp16 [K/128, N]."""
     n = wq_kernel.shape[1]
     return _gemm(_lib.lib().cf_w4a16_gemm, x, wq_kernel, scales, n, residual, out, split_k, workspace, status,
-                 True, timeout_ns, stream)
+                 True, timeout_ns, stream, trace)
 
 
 def dense_gemm(x: torch.Tensor, w: torch.Tensor, *, residual=None, out=None, split_k: int = 0, workspace=None,

@@ -168,6 +168,8 @@ typedef struct cf_gemm_args {
   size_t workspace_bytes;
   int32_t *status;       /* optional */
   uint64_t timeout_ns;   /* 0 = default */
+  uint64_t *trace;       /* optional profiling aid: [6][512] global-timer stamps of CTA 0
+                            (W issue, dequant start/end, MMA issue, X issue, epilogue) */
 } cf_gemm_args;
 
 size_t cf_gemm_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t split_k, int32_t int4);
