@@ -27,6 +27,7 @@
 #include "tmap.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <math.h>
 
 namespace {
@@ -34,7 +35,6 @@ namespace {
 using namespace cf::sm100;
 
 constexpr int kPage = 16;   // tokens per KV page (reference block_size 16)
-constexpr int kStages = 4;
 constexpr uint64_t kDrainNs = 1000000000ull;
 
 struct AttnParams {
@@ -105,27 +105,40 @@ __device__ __forceinline__ uint32_t q_off(int r, int c) {
   return (uint32_t)(r * (HD * 2) + ((c ^ (r & 7)) << 4));
 }
 
-template <typename T, int HD, int NW>
-__global__ void __launch_bounds__(NW * 32)
+// One CTA = 16*MT query rows (one row tile of a kv-head group) x one KV
+// split.  Warp 4 is the producer: it keeps a CTA-wide ring of kStages pages
+// full (each page's four 64-column TMA boxes issued by four of its lanes; the
+// split's new-row tiles copied in with plain loads).  Consumer warps 0-3 take
+// the pages round-robin, each with its own online-softmax state over the
+// CTA's rows, and release every slot through an `empty` barrier, so the only
+// CTA-wide barriers are before and after the page loop; the four partial
+// states are merged in shared memory at the end.
+constexpr int kConsumers = 4;
+
+template <typename T, int HD, int MTW, int kStages>
+__global__ void __launch_bounds__((kConsumers * MTW + 1) * 32, 2)
 verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                    const AttnParams p) {
-  constexpr int ROWS = 16 * NW;
   constexpr int TILE_BYTES = kPage * HD * 2;  // one tensor, one page
   constexpr int CH = HD / 8;                  // 16-B chunks per row
+  constexpr int NBOX = HD / 64;               // 64-column TMA boxes per tile
+  constexpr int kRows = 16 * MTW;
+  constexpr int MT = 1;  // m16 tiles per consumer warp
+  constexpr int kThreadsAll = (kConsumers * MTW + 1) * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *kv_s = smem;                                   // [kStages][K tile, V tile]
-  uint8_t *q_s = smem + kStages * 2 * TILE_BYTES;         // [ROWS][HD]
-  uint64_t *full = reinterpret_cast<uint64_t *>(q_s + ROWS * HD * 2);
-  __shared__ int s_abort;
+  uint8_t *kv_s = smem;                                           // [stage][K, V]
+  uint8_t *q_s = smem + kStages * 2 * TILE_BYTES;                 // [rows][HD]
+  uint64_t *full = reinterpret_cast<uint64_t *>(q_s + kRows * HD * 2);
+  uint64_t *empty = full + kStages;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row_tile = blockIdx.x;
   const int b = blockIdx.y / p.Hkv, h = blockIdx.y % p.Hkv;
   const int split = blockIdx.z;
   const int ctx = p.context_lens[b];
-  const int pc = (ctx + kPage - 1) / kPage;       // cached pages
-  const int pn = (p.R + kPage - 1) / kPage;       // new-row tiles
+  const int pc = (ctx + kPage - 1) / kPage;  // cached pages
+  const int pn = (p.R + kPage - 1) / kPage;  // new-row tiles
   const int T_all = pc + pn;
   const int tps = (T_all + p.nsplit - 1) / p.nsplit;
   const int t_begin = min(T_all, split * tps), t_end = min(T_all, t_begin + tps);
@@ -133,14 +146,13 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
   const int32_t *btab = p.block_tables + (int64_t)b * p.max_blocks;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], MTW); }
     fence_mbar_init();
-    s_abort = 0;
   }
   // ---- Q tile -> shared (rows >= R*G are zero) ----
-  for (int idx = tid; idx < ROWS * CH; idx += NW * 32) {
+  for (int idx = tid; idx < kRows * CH; idx += kThreadsAll) {
     const int r = idx / CH, c = idx % CH;
-    const int qrow = row_tile * ROWS + r;
+    const int qrow = row_tile * kRows + r;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (qrow < p.rows_total) {
       const int rr = qrow / p.G, g = qrow % p.G;
@@ -152,148 +164,174 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
   }
   __syncthreads();
 
-  // ---- producer: TMA of cached page i (of this split) into stage i % kStages ----
-  const int pool_rows_per_block = p.L * p.Hkv * kPage;
-  auto issue = [&](int i) {
-    const int t = t_begin + i;
-    if (t >= pc) return;  // new-row tiles are copied by all threads
-    const int s = i % kStages;
-    int blk = btab[t];
-    if (blk < 0 || blk >= p.total_blocks) {  // invalid page id: record and load page 0 (masked below)
-      if (p.status) atomicExch(p.status, CF_ERANGE);
-      blk = 0;
-    }
-    const int y = blk * pool_rows_per_block + (p.layer * p.Hkv + h) * kPage;
-    uint8_t *st = kv_s + s * 2 * TILE_BYTES;
-    mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
+  bool abort = false;
+  float o[MT][HD / 8][4];
+  float m_r[2 * MT], l_r[2 * MT];
 #pragma unroll
-    for (int half = 0; half < HD / 64; ++half) {
-      tma_load_2d(st + half * kPage * 128, &tm_k, &full[s], half * 64, y);
-      tma_load_2d(st + TILE_BYTES + half * kPage * 128, &tm_v, &full[s], half * 64, y);
-    }
-  };
-  int issued = 0;
-  if (tid == 0) {
-    for (int i = 0; i < kStages - 1 && i < ntiles; ++i) { issue(i); issued = i + 1; }
-  }
-
-  // ---- per-warp state ----
-  float o[HD / 8][4];
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-  for (int d = 0; d < HD / 8; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.0f;
-  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
-  const int wrow0 = warp * 16;
-  const int qrow_a = row_tile * ROWS + wrow0 + (lane >> 2);  // rows of c0,c1 / c2,c3: +0 / +8
-  const bool warp_active = row_tile * ROWS + wrow0 < p.rows_total;
-  const uint32_t q_base = smem_u32(q_s);
+    for (int d = 0; d < HD / 8; ++d) o[mt][d][0] = o[mt][d][1] = o[mt][d][2] = o[mt][d][3] = 0.0f;
+#pragma unroll
+  for (int hr = 0; hr < 2 * MT; ++hr) { m_r[hr] = -INFINITY; l_r[hr] = 0.0f; }
 
-  for (int i = 0; i < ntiles; ++i) {
-    const int t = t_begin + i;
-    const int s = i % kStages;
-    uint8_t *st = kv_s + s * 2 * TILE_BYTES;
-    if (tid == 0 && i + kStages - 1 < ntiles) { issue(i + kStages - 1); issued = i + kStages; }
-    if (t < pc) {
-      if (!mbar_wait(&full[s], (uint32_t)(i / kStages) & 1u, p.timeout_ns)) s_abort = 1;
-    } else {
-      // new rows (t - pc)*16 .. : copy this step's K/V scratch rows into the stage
-      const int j0 = (t - pc) * kPage;
-      for (int idx = tid; idx < kPage * CH; idx += NW * 32) {
-        const int r = idx / CH, c = idx % CH;
-        const int j = j0 + r;
-        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-        if (j < p.R) {
-          const int64_t off = ((int64_t)(b * p.R + j) * p.Hkv + h) * HD + c * 8;
-          kv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.k_new) + off);
-          vv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.v_new) + off);
+  const int cw = warp % kConsumers;      // page stream of a consumer warp
+  const int mrow0 = (warp / kConsumers) * 16;  // its m16 tile within the CTA rows
+  if (warp == kConsumers * MTW) {
+    // ---------------- producer ----------------
+    const int pool_rows_per_block = p.L * p.Hkv * kPage;
+    int issued = 0;
+    for (int j = 0; j < ntiles; ++j) {
+      const int t = t_begin + j;
+      const int s = j % kStages;
+      if (j >= kStages && !mbar_wait_warp(&empty[s], ((uint32_t)(j / kStages) & 1u) ^ 1u, p.timeout_ns)) {
+        abort = true;
+        break;
+      }
+      uint8_t *st = kv_s + s * 2 * TILE_BYTES;
+      if (t < pc) {
+        int blk = btab[t];
+        if (blk < 0 || blk >= p.total_blocks) {  // invalid page id: record and read page 0 (masked below)
+          if (p.status && lane == 0) atomicExch(p.status, CF_ERANGE);
+          blk = 0;
         }
-        *reinterpret_cast<uint4 *>(st + kv_off<HD>(r, c)) = kv;
-        *reinterpret_cast<uint4 *>(st + TILE_BYTES + kv_off<HD>(r, c)) = vv;
+        const int y = blk * pool_rows_per_block + (p.layer * p.Hkv + h) * kPage;
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
+        __syncwarp();
+        if (lane < NBOX) tma_load_2d(st + lane * kPage * 128, &tm_k, &full[s], lane * 64, y);
+        else if (lane < 2 * NBOX)
+          tma_load_2d(st + TILE_BYTES + (lane - NBOX) * kPage * 128, &tm_v, &full[s], (lane - NBOX) * 64, y);
+        issued = j + 1;
+      } else {
+        // new rows (t - pc)*16 ..: this step's K/V scratch rows (plain loads)
+        const int j0 = (t - pc) * kPage;
+        for (int idx = lane; idx < kPage * CH; idx += 32) {
+          const int r = idx / CH, c = idx % CH;
+          const int jr = j0 + r;
+          uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+          if (jr < p.R) {
+            const int64_t off = ((int64_t)(b * p.R + jr) * p.Hkv + h) * HD + c * 8;
+            kv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.k_new) + off);
+            vv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.v_new) + off);
+          }
+          *reinterpret_cast<uint4 *>(st + kv_off<HD>(r, c)) = kv;
+          *reinterpret_cast<uint4 *>(st + TILE_BYTES + kv_off<HD>(r, c)) = vv;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);  // release: the rows are visible to the consumer
       }
     }
-    __syncthreads();
-    if (s_abort) break;
-    if (warp_active) {
-      const uint32_t k_base = smem_u32(st), v_base = k_base + TILE_BYTES;
-      // S = Q K^T for this warp's 16 rows x 16 tokens
-      float sc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    if (abort)  // let our own copies land before the CTA can exit
+      for (int jj = max(0, issued - kStages); jj < issued; ++jj)
+        if (t_begin + jj < pc) mbar_wait_warp(&full[jj % kStages], (uint32_t)(jj / kStages) & 1u, kDrainNs);
+  } else {
+    // ---------------- consumers: page j goes to the MTW warps of stream j % 4 ----------------
+    const uint32_t q_base = smem_u32(q_s);
+    for (int j = cw; j < ntiles; j += kConsumers) {
+      const int t = t_begin + j;
+      const int s = j % kStages;
+      if (!mbar_wait_warp(&full[s], (uint32_t)(j / kStages) & 1u, p.timeout_ns)) { abort = true; break; }
+      const uint32_t k_base = smem_u32(kv_s + s * 2 * TILE_BYTES), v_base = k_base + TILE_BYTES;
+      // S = Q K^T: rows x 16 tokens
+      float sc[MT][2][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) sc[mt][nt][0] = sc[mt][nt][1] = sc[mt][nt][2] = sc[mt][nt][3] = 0.0f;
 #pragma unroll
       for (int kk = 0; kk < HD / 16; ++kk) {
-        uint32_t a[4], kb[4];
-        {
-          const int r = wrow0 + (lane & 7) + ((lane >> 3) & 1) * 8;
-          const int c = 2 * kk + (lane >> 4);
-          ldsm_x4(q_base + q_off<HD>(r, c), a);
-        }
+        uint32_t kb[4];
         {
           const int tok = ((lane >> 4) << 3) + (lane & 7);
           const int c = 2 * kk + ((lane >> 3) & 1);
           ldsm_x4(k_base + kv_off<HD>(tok, c), kb);
         }
-        MmaOp<T>::run(sc[0], a, kb[0], kb[1]);
-        MmaOp<T>::run(sc[1], a, kb[2], kb[3]);
-      }
-      // mask + online softmax (log2 domain)
-      float mx[2] = {m_r[0], m_r[1]};
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int col = nt * 8 + 2 * (lane & 3) + (e & 1);
-          const int qrow = qrow_a + (e >> 1) * 8;
-          bool vis;
-          if (t < pc) {
-            vis = t * kPage + col < ctx;
-          } else {
-            const int j = (t - pc) * kPage + col;
-            const int rq = qrow / p.G;
-            if (j >= p.R || qrow >= p.rows_total) {
-              vis = false;
-            } else if (p.tree_mask) {
-              const uint64_t w = p.tree_mask[((int64_t)b * p.R + rq) * p.mask_words + (j >> 6)];
-              vis = (w >> (j & 63)) & 1ull;
-            } else {
-              vis = j <= rq;
-            }
-          }
-          const float x = vis ? sc[nt][e] * p.scale_log2 : -INFINITY;
-          sc[nt][e] = x;
-          mx[e >> 1] = fmaxf(mx[e >> 1], x);
+        for (int mt = 0; mt < MT; ++mt) {
+          uint32_t a[4];
+          const int r = mrow0 + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int c = 2 * kk + (lane >> 4);
+          ldsm_x4(q_base + q_off<HD>(r, c), a);
+          MmaOp<T>::run(sc[mt][0], a, kb[0], kb[1]);
+          MmaOp<T>::run(sc[mt][1], a, kb[2], kb[3]);
         }
       }
+      // mask + online softmax (log2 domain); row index hr = mt*2 + (e>>1)
+      const bool full_page = (t + 1) * kPage <= ctx;  // cached page with all 16 slots valid
+      float mx[2 * MT];
 #pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
+      for (int hr = 0; hr < 2 * MT; ++hr) mx[hr] = m_r[hr];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            bool vis = true;
+            if (!full_page) {
+              const int col = nt * 8 + 2 * (lane & 3) + (e & 1);
+              const int qrow = row_tile * kRows + mrow0 + mt * 16 + (lane >> 2) + (e >> 1) * 8;
+              if (t < pc) {
+                vis = t * kPage + col < ctx;
+              } else {
+                const int jr = (t - pc) * kPage + col;
+                const int rq = qrow / p.G;
+                if (jr >= p.R || qrow >= p.rows_total) {
+                  vis = false;
+                } else if (p.tree_mask) {
+                  const uint64_t w = p.tree_mask[((int64_t)b * p.R + rq) * p.mask_words + (jr >> 6)];
+                  vis = (w >> (jr & 63)) & 1ull;
+                } else {
+                  vis = jr <= rq;
+                }
+              }
+            }
+            const float x = vis ? sc[mt][nt][e] * p.scale_log2 : -INFINITY;
+            sc[mt][nt][e] = x;
+            const int hr = mt * 2 + (e >> 1);
+            mx[hr] = fmaxf(mx[hr], x);
+          }
+#pragma unroll
+      for (int hr = 0; hr < 2 * MT; ++hr) {
         mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
         mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
       }
-      float corr[2];
+      float corr[2 * MT];
+      bool moved = false;
 #pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
+      for (int hr = 0; hr < 2 * MT; ++hr) {
         corr[hr] = (m_r[hr] == -INFINITY) ? 0.0f : exp2f(m_r[hr] - mx[hr]);
         if (mx[hr] == -INFINITY) corr[hr] = 1.0f;
+        moved |= corr[hr] != 1.0f;
         m_r[hr] = mx[hr];
         l_r[hr] *= corr[hr];
       }
-      uint32_t pa[4];
-      {
+      uint32_t pa[MT][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
         float pv[2][4];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float mm = m_r[e >> 1];
-            const float pe = (mm == -INFINITY) ? 0.0f : exp2f(sc[nt][e] - mm);
+            const int hr = mt * 2 + (e >> 1);
+            const float pe = (m_r[hr] == -INFINITY) ? 0.0f : exp2f(sc[mt][nt][e] - m_r[hr]);
             pv[nt][e] = pe;
-            l_r[e >> 1] += pe;
+            l_r[hr] += pe;
           }
-        pa[0] = MmaOp<T>::pack(pv[0][0], pv[0][1]);
-        pa[1] = MmaOp<T>::pack(pv[0][2], pv[0][3]);
-        pa[2] = MmaOp<T>::pack(pv[1][0], pv[1][1]);
-        pa[3] = MmaOp<T>::pack(pv[1][2], pv[1][3]);
+        pa[mt][0] = MmaOp<T>::pack(pv[0][0], pv[0][1]);
+        pa[mt][1] = MmaOp<T>::pack(pv[0][2], pv[0][3]);
+        pa[mt][2] = MmaOp<T>::pack(pv[1][0], pv[1][1]);
+        pa[mt][3] = MmaOp<T>::pack(pv[1][2], pv[1][3]);
       }
+      // rescale O only when some row's running max moved (rare after the first pages)
+      if (__any_sync(0xffffffffu, moved)) {
 #pragma unroll
-      for (int d = 0; d < HD / 8; ++d) {
-        o[d][0] *= corr[0]; o[d][1] *= corr[0];
-        o[d][2] *= corr[1]; o[d][3] *= corr[1];
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int d = 0; d < HD / 8; ++d) {
+            o[mt][d][0] *= corr[mt * 2]; o[mt][d][1] *= corr[mt * 2];
+            o[mt][d][2] *= corr[mt * 2 + 1]; o[mt][d][3] *= corr[mt * 2 + 1];
+          }
       }
       // O += P V
 #pragma unroll
@@ -302,48 +340,69 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
         const int tok = (((lane >> 3) & 1) << 3) + (lane & 7);
         const int c = 2 * dp + (lane >> 4);
         ldsm_x4_t(v_base + kv_off<HD>(tok, c), vb);
-        MmaOp<T>::run(o[2 * dp], pa, vb[0], vb[1]);
-        MmaOp<T>::run(o[2 * dp + 1], pa, vb[2], vb[3]);
-      }
-    }
-    __syncthreads();  // stage s is free for the prefetch issued next iteration
-  }
-
-  if (s_abort) {
-    if (p.status) atomicExch(p.status, CF_ETIMEOUT);
-    if (tid == 0)  // let our own copies land before the CTA exits
-      for (int j = max(0, issued - kStages); j < issued; ++j)
-        if (t_begin + j < pc) mbar_wait(&full[j % kStages], (uint32_t)(j / kStages) & 1u, kDrainNs);
-    return;
-  }
-  if (!warp_active) return;
 #pragma unroll
-  for (int hr = 0; hr < 2; ++hr) {
+        for (int mt = 0; mt < MT; ++mt) {
+          MmaOp<T>::run(o[mt][2 * dp], pa[mt], vb[0], vb[1]);
+          MmaOp<T>::run(o[mt][2 * dp + 1], pa[mt], vb[2], vb[3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // slot s may be refilled
+    }
+  }
+  if (abort && p.status && lane == 0) atomicExch(p.status, CF_ETIMEOUT);
+  const int any_abort = __syncthreads_or(abort ? 1 : 0);
+  // ---- merge the consumers' (m, l, O) per row in shared memory ----
+#pragma unroll
+  for (int hr = 0; hr < 2 * MT; ++hr) {
     l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 1);
     l_r[hr] += __shfl_xor_sync(0xffffffffu, l_r[hr], 2);
   }
+  float *so = reinterpret_cast<float *>(kv_s);            // [stream][rows][HD]
+  float *sm_ = so + kConsumers * kRows * HD;                // [stream][rows]
+  float *sl = sm_ + kConsumers * kRows;                     // [stream][rows]
+  if (warp < kConsumers * MTW)  // the producer holds no softmax state
 #pragma unroll
-  for (int hr = 0; hr < 2; ++hr) {
-    const int qrow = qrow_a + hr * 8;
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int e2 = 0; e2 < 2; ++e2) {
+      const int r = mrow0 + mt * 16 + (lane >> 2) + e2 * 8;
+      float *dst = so + (cw * kRows + r) * HD;
+#pragma unroll
+      for (int d = 0; d < HD / 8; ++d)
+        *reinterpret_cast<float2 *>(dst + d * 8 + 2 * (lane & 3)) = make_float2(o[mt][d][2 * e2], o[mt][d][2 * e2 + 1]);
+      if ((lane & 3) == 0) { sm_[cw * kRows + r] = abort ? -INFINITY : m_r[mt * 2 + e2]; sl[cw * kRows + r] = l_r[mt * 2 + e2]; }
+    }
+  __syncthreads();
+  if (any_abort) return;
+  for (int idx = tid; idx < kRows * HD; idx += kThreadsAll) {
+    const int r = idx / HD, d = idx % HD;
+    const int qrow = row_tile * kRows + r;
     if (qrow >= p.rows_total) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, sm_[w * kRows + r]);
+    float num = 0.0f, den = 0.0f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kConsumers; ++w) {
+        const float mw = sm_[w * kRows + r];
+        if (mw == -INFINITY) continue;
+        const float f = exp2f(mw - M);
+        num += f * so[(w * kRows + r) * HD + d];
+        den += f * sl[w * kRows + r];
+      }
+    }
     const int rr = qrow / p.G, g = qrow % p.G;
-    const float inv = l_r[hr] > 0.0f ? 1.0f / l_r[hr] : 0.0f;
     if (p.nsplit == 1) {
       T *dst = reinterpret_cast<T *>(p.out) + (int64_t)(b * p.R + rr) * p.out_row_stride + (int64_t)(h * p.G + g) * HD;
-#pragma unroll
-      for (int d = 0; d < HD / 8; ++d) {
-        const int col = d * 8 + 2 * (lane & 3);
-        *reinterpret_cast<uint32_t *>(dst + col) = MmaOp<T>::pack(o[d][2 * hr] * inv, o[d][2 * hr + 1] * inv);
-      }
+      const float v = den > 0.0f ? num / den : 0.0f;
+      if constexpr (std::is_same<T, __half>::value) dst[d] = __float2half_rn(v);
+      else dst[d] = __float2bfloat16_rn(v);
     } else {
       const int64_t rowid = (((int64_t)split * p.B + b) * p.Hkv + h) * p.rows_total + qrow;
-      float *dst = p.ws_o + rowid * HD;
-#pragma unroll
-      for (int d = 0; d < HD / 8; ++d) {
-        const int col = d * 8 + 2 * (lane & 3);
-        *reinterpret_cast<float2 *>(dst + col) = make_float2(o[d][2 * hr] * inv, o[d][2 * hr + 1] * inv);
-      }
-      if ((lane & 3) == 0) p.ws_lse[rowid] = (l_r[hr] > 0.0f) ? m_r[hr] + log2f(l_r[hr]) : -INFINITY;
+      p.ws_o[rowid * HD + d] = den > 0.0f ? num / den : 0.0f;
+      if (d == 0) p.ws_lse[rowid] = den > 0.0f ? M + log2f(den) : -INFINITY;
     }
   }
 }
@@ -374,6 +433,11 @@ __global__ void attn_combine_kernel(const AttnParams p) {
   }
 }
 
+int attn_mt() {
+  const char *v = getenv("CF_ATTN_MT");
+  return v ? atoi(v) : 2;
+}
+
 int pick_splits(const cf_attn_args &a, int row_tiles) {
   if (a.num_splits > 0) return a.num_splits;
   int sms = 148;
@@ -381,14 +445,15 @@ int pick_splits(const cf_attn_args &a, int row_tiles) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int ctas = a.batch * a.kv.num_kv_heads * row_tiles;
-  const int want = (4 * sms + ctas - 1) / ctas;
+  // two resident CTAs per SM: split the context only when the grid would not fill them
+  const int want = ctas >= 2 * sms ? 1 : (2 * sms + ctas - 1) / ctas;
   const int pages = (a.max_context + kPage - 1) / kPage;
   return std::max(1, std::min(want, std::max(1, pages / 8)));
 }
 
-template <typename T, int HD, int NW>
+template <typename T, int HD, int MT, int kStages>
 int launch(const cf_attn_args &a, cudaStream_t stream) {
-  constexpr int ROWS = 16 * NW;
+  constexpr int ROWS = 16 * MT;
   const int G = a.num_q_heads / a.kv.num_kv_heads;
   AttnParams p;
   p.B = a.batch; p.R = a.rows; p.G = G; p.Hkv = a.kv.num_kv_heads; p.L = a.kv.num_layers; p.layer = a.layer;
@@ -424,11 +489,15 @@ int launch(const cf_attn_args &a, cudaStream_t stream) {
   if (!cf::make_tmap_2d(&tk, tdt, a.kv.key_pool, HD, pool_rows, HD * 2, 64, kPage, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !cf::make_tmap_2d(&tv, tdt, a.kv.val_pool, HD, pool_rows, HD * 2, 64, kPage, CU_TENSOR_MAP_SWIZZLE_128B))
     return CF_EINVAL;
-  const size_t smem = 1024 + kStages * 2 * kPage * HD * 2 + ROWS * HD * 2 + kStages * 8;
-  auto kern = verify_attn_kernel<T, HD, NW>;
+  // the stage area is reused for the merge: [4][rows][HD] fp32 + m, l
+  const size_t stage_area = std::max<size_t>((size_t)kStages * 2 * kPage * HD * 2,
+                                             (size_t)kConsumers * ROWS * (HD + 2) * 4);
+  const size_t smem = 1024 + stage_area + ROWS * HD * 2 + kStages * 16;
+  auto kern = verify_attn_kernel<T, HD, MT, kStages>;
   CF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
   dim3 grid(row_tiles, p.B * p.Hkv, p.nsplit);
-  kern<<<grid, NW * 32, smem, stream>>>(tk, tv, p);
+  kern<<<grid, (kConsumers * MT + 1) * 32, smem, stream>>>(tk, tv, p);
   if (cudaGetLastError() != cudaSuccess) return CF_ECUDA;
   if (p.nsplit > 1) {
     dim3 g2(p.B * p.Hkv, p.rows_total);
@@ -439,10 +508,9 @@ int launch(const cf_attn_args &a, cudaStream_t stream) {
 
 template <typename T>
 int dispatch(const cf_attn_args &a, cudaStream_t s) {
-  const int G = a.num_q_heads / a.kv.num_kv_heads;
-  const bool small = a.rows * G <= 32;
-  if (a.kv.head_dim == 128) return small ? launch<T, 128, 2>(a, s) : launch<T, 128, 4>(a, s);
-  if (a.kv.head_dim == 64) return small ? launch<T, 64, 2>(a, s) : launch<T, 64, 4>(a, s);
+  const int mt = attn_mt();
+  if (a.kv.head_dim == 128) return mt == 2 ? launch<T, 128, 2, 8>(a, s) : launch<T, 128, 1, 8>(a, s);
+  if (a.kv.head_dim == 64) return mt == 2 ? launch<T, 64, 2, 8>(a, s) : launch<T, 64, 1, 8>(a, s);
   return CF_EUNSUPPORTED;
 }
 
@@ -452,7 +520,7 @@ extern "C" size_t cf_attention_workspace_bytes(const cf_attn_args *a) {
   if (!a || a->kv.num_kv_heads <= 0 || a->num_q_heads % a->kv.num_kv_heads) return 0;
   const int G = a->num_q_heads / a->kv.num_kv_heads;
   const int rows_total = a->rows * G;
-  const int ROWS = rows_total <= 32 ? 32 : 64;
+  const int ROWS = 16 * attn_mt();
   const int nsplit = pick_splits(*a, (rows_total + ROWS - 1) / ROWS);
   if (nsplit <= 1) return 0;
   const size_t rows = (size_t)nsplit * a->batch * a->kv.num_kv_heads * rows_total;

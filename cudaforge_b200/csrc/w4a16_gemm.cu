@@ -73,7 +73,6 @@ struct GemmParams {
   int *status;
   uint64_t timeout_ns;
   unsigned long long *trace;
-  int dbg_nox;
 };
 
 // 8 repacked nibbles -> 8 bf16 (k order 0..7).  Repacked nibble position p
@@ -202,13 +201,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       // sustains only ~30 GB/s of TMA traffic, many lanes in parallel far more
       if (lane == 0) {
         CF_TRACE(4, i);
-        mbar_arrive_expect_tx(&xfull[s], (p.dbg_nox & 1) ? 0 : p.x_bytes);
+        mbar_arrive_expect_tx(&xfull[s], p.x_bytes);
       }
       __syncwarp();
       {
         const int nbox = p.m_slice / 16;
         const int b = (lane - i * nbox) & 31;  // box handled by this lane (rotating per stage)
-        if (!(p.dbg_nox & 1) && b < nbox)
+        if (b < nbox)
           tma_load_2d(x_ring + s * p.x_bytes + b * 2048, &tm_x, &xfull[s], kb * BK, m0 + b * 16);
       }
       __syncwarp();
@@ -231,7 +230,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       const uint32_t x_base = smem_u32(x_ring + sx * p.x_bytes);
       if (elect_one()) {
         CF_TRACE(3, i);
-        if (!(p.dbg_nox & 8))
         for (int k16 = 0; k16 < BK / 16; ++k16) {
           const uint64_t bd = desc_kmajor_sw128(x_base + k16 * 32);
           for (int h = 0; h < halves; ++h) {
@@ -279,17 +277,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         __syncwarp();
         if (lane == 0) mbar_arrive(&wempty[sw]);  // packed words are in registers
         uint32_t a[32];
-        if (!(p.dbg_nox & 4)) {
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint4 v = dequant8(w[kk], s2);
-            a[4 * kk + 0] = v.x; a[4 * kk + 1] = v.y; a[4 * kk + 2] = v.z; a[4 * kk + 3] = v.w;
-          }
-        } else {
-#pragma unroll
-          for (int kk = 0; kk < 32; ++kk) a[kk] = w[kk & 7];
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint4 v = dequant8(w[kk], s2);
+          a[4 * kk + 0] = v.x; a[4 * kk + 1] = v.y; a[4 * kk + 2] = v.z; a[4 * kk + 3] = v.w;
         }
-        if (h < halves && !(p.dbg_nox & 2))
+        if (h < halves)
           tmem_st_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + p.a_tcol + (uint32_t)((sa * 2 + h) * 32), a);
         tmem_st_wait();
         tc_fence_before();
@@ -505,7 +498,6 @@ int run_gemm(const cf_gemm_args &a, cudaStream_t stream) {
   p.off_x = pl.off_x; p.off_w = pl.off_w; p.off_bar = pl.off_bar; p.x_bytes = pl.x_bytes;
   p.tmem_cols = pl.tmem_cols;
   p.a_tcol = pl.a_tcol;
-  p.dbg_nox = getenv("CF_GEMM_DBG") ? atoi(getenv("CF_GEMM_DBG")) : 0;
   p.idesc = cf::sm100::idesc_bf16_f32(HN, pl.m_slice);
   if (std::is_same<T, __half>::value) p.idesc &= ~((7u << 7) | (7u << 10));  // A, B format f16
   p.y = a.y; p.ldy = a.ldy; p.residual = a.residual; p.ldr = a.ldr;
