@@ -231,20 +231,14 @@ def run_ours(args):
         e2e_tokens += int((h_out_n.clamp_min(0) + 1).sum())
     x1.record()
     barrier()
-    e2e_ms = x1.elapsed_time(x0) * -1 if False else x0.elapsed_time(x1)
+    e2e_ms = x0.elapsed_time(x1)
     h2d = dtok.numel() * 4 + B * (K + 1) * 4
     d2h = B * R * 4 + B * 4
 
-    # max over ranks
-    t = torch.tensor([ms, e2e_ms, float(sum(tokens_per_step)), float(e2e_tokens)], device=device, dtype=torch.float64)
-    if world > 1:
-        tm = t.clone()
-        dist.all_reduce(tm[:2], op=dist.ReduceOp.MAX)
-        ts = t.clone()
-        dist.all_reduce(ts[2:], op=dist.ReduceOp.SUM)
-        ms_max, e2e_max, tok_all, e2e_tok_all = tm[0].item(), tm[1].item(), ts[2].item(), ts[3].item()
-    else:
-        ms_max, e2e_max, tok_all, e2e_tok_all = ms, e2e_ms, float(sum(tokens_per_step)), float(e2e_tokens)
+    # max over ranks of the device times, sum of the emitted tokens (batch-sharded, no data-path collective)
+    from cudaforge_b200.shard import reduce_step_metrics
+    (ms_max, e2e_max), (tok_all, e2e_tok_all) = reduce_step_metrics(
+        [ms, e2e_ms], [float(sum(tokens_per_step)), float(e2e_tokens)], device=device)
     value = tok_all / (ms_max / 1e3)
     e2e_value = e2e_tok_all / (e2e_max / 1e3)
 
