@@ -57,7 +57,7 @@ class CfAttnArgs(ctypes.Structure):
         ("block_tables", _P), ("max_blocks", _I32), ("context_lens", _P), ("max_context", _I32),
         ("tree_mask", _P), ("mask_words", _I32), ("out", _P), ("out_row_stride", _I64), ("scale", _F32),
         ("num_splits", _I32), ("workspace", _P), ("workspace_bytes", ctypes.c_size_t), ("status", _P),
-        ("timeout_ns", ctypes.c_uint64),
+        ("timeout_ns", ctypes.c_uint64), ("trace", _P),
     ]
 
 

@@ -52,6 +52,7 @@ struct AttnParams {
   float *ws_o, *ws_lse;
   int *status;
   uint64_t timeout_ns;
+  unsigned long long *trace;
 };
 
 template <typename T> struct MmaOp;
@@ -81,6 +82,13 @@ template <> struct MmaOp<__half> {
     return *reinterpret_cast<uint32_t *>(&v);
   }
 };
+
+// Hardware base-2 exponential (MUFU), flush-to-zero; ex2(-inf) = +0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -144,6 +152,8 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
   const int t_begin = min(T_all, split * tps), t_end = min(T_all, t_begin + tps);
   const int ntiles = t_end - t_begin;
   const int32_t *btab = p.block_tables + (int64_t)b * p.max_blocks;
+  const bool tr = p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+  if (tr && tid == 0) p.trace[3072] = clock64();
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], MTW); }
@@ -183,11 +193,12 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
     for (int j = 0; j < ntiles; ++j) {
       const int t = t_begin + j;
       const int s = j % kStages;
-      if (j >= kStages && !mbar_wait_warp(&empty[s], ((uint32_t)(j / kStages) & 1u) ^ 1u, p.timeout_ns)) {
+      if (j >= kStages && !mbar_wait_warp_sleep(&empty[s], ((uint32_t)(j / kStages) & 1u) ^ 1u, p.timeout_ns)) {
         abort = true;
         break;
       }
       uint8_t *st = kv_s + s * 2 * TILE_BYTES;
+      if (tr && lane == 0 && j < 1024) p.trace[j] = clock64();
       if (t < pc) {
         int blk = btab[t];
         if (blk < 0 || blk >= p.total_blocks) {  // invalid page id: record and read page 0 (masked below)
@@ -229,7 +240,8 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
     for (int j = cw; j < ntiles; j += kConsumers) {
       const int t = t_begin + j;
       const int s = j % kStages;
-      if (!mbar_wait_warp(&full[s], (uint32_t)(j / kStages) & 1u, p.timeout_ns)) { abort = true; break; }
+      if (!mbar_wait_warp_sleep(&full[s], (uint32_t)(j / kStages) & 1u, p.timeout_ns)) { abort = true; break; }
+      if (tr && lane == 0 && mrow0 == 0 && j < 1024) p.trace[1024 + j] = clock64();
       const uint32_t k_base = smem_u32(kv_s + s * 2 * TILE_BYTES), v_base = k_base + TILE_BYTES;
       // S = Q K^T: rows x 16 tokens
       float sc[MT][2][4];
@@ -255,21 +267,19 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
           MmaOp<T>::run(sc[mt][1], a, kb[2], kb[3]);
         }
       }
-      // mask + online softmax (log2 domain); row index hr = mt*2 + (e>>1)
+      // mask (partial pages only) + online softmax in the log2 domain:
+      // p = 2^(s * scale - m) with one FFMA + one hardware ex2 per element.
       const bool full_page = (t + 1) * kPage <= ctx;  // cached page with all 16 slots valid
-      float mx[2 * MT];
+      if (!full_page) {
 #pragma unroll
-      for (int hr = 0; hr < 2 * MT; ++hr) mx[hr] = m_r[hr];
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
+          for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            bool vis = true;
-            if (!full_page) {
+            for (int e = 0; e < 4; ++e) {
               const int col = nt * 8 + 2 * (lane & 3) + (e & 1);
               const int qrow = row_tile * kRows + mrow0 + mt * 16 + (lane >> 2) + (e >> 1) * 8;
+              bool vis;
               if (t < pc) {
                 vis = t * kPage + col < ctx;
               } else {
@@ -284,24 +294,30 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
                   vis = jr <= rq;
                 }
               }
+              if (!vis) sc[mt][nt][e] = -INFINITY;
             }
-            const float x = vis ? sc[mt][nt][e] * p.scale_log2 : -INFINITY;
-            sc[mt][nt][e] = x;
-            const int hr = mt * 2 + (e >> 1);
-            mx[hr] = fmaxf(mx[hr], x);
-          }
+      }
+      float mx[2 * MT];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2) {
+          const float raw = fmaxf(fmaxf(sc[mt][0][2 * e2], sc[mt][0][2 * e2 + 1]),
+                                  fmaxf(sc[mt][1][2 * e2], sc[mt][1][2 * e2 + 1]));
+          mx[mt * 2 + e2] = raw;
+        }
 #pragma unroll
       for (int hr = 0; hr < 2 * MT; ++hr) {
         mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
         mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
+        mx[hr] = fmaxf(m_r[hr], mx[hr] * p.scale_log2);  // new running max (log2 units)
       }
       float corr[2 * MT];
       bool moved = false;
 #pragma unroll
       for (int hr = 0; hr < 2 * MT; ++hr) {
-        corr[hr] = (m_r[hr] == -INFINITY) ? 0.0f : exp2f(m_r[hr] - mx[hr]);
-        if (mx[hr] == -INFINITY) corr[hr] = 1.0f;
-        moved |= corr[hr] != 1.0f;
+        corr[hr] = (mx[hr] == m_r[hr]) ? 1.0f : ex2_approx(m_r[hr] - mx[hr]);  // -inf - x -> 0
+        moved |= mx[hr] != m_r[hr];
         m_r[hr] = mx[hr];
         l_r[hr] *= corr[hr];
       }
@@ -314,7 +330,9 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int hr = mt * 2 + (e >> 1);
-            const float pe = (m_r[hr] == -INFINITY) ? 0.0f : exp2f(sc[mt][nt][e] - m_r[hr]);
+            // a row that has seen only masked keys keeps m = -inf: its p must be 0
+            const float pe = (m_r[hr] == -INFINITY) ? 0.0f
+                                                    : ex2_approx(fmaf(sc[mt][nt][e], p.scale_log2, -m_r[hr]));
             pv[nt][e] = pe;
             l_r[hr] += pe;
           }
@@ -348,10 +366,12 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);  // slot s may be refilled
+      if (tr && lane == 0 && mrow0 == 0 && j < 1024) p.trace[2048 + j] = clock64();
     }
   }
   if (abort && p.status && lane == 0) atomicExch(p.status, CF_ETIMEOUT);
   const int any_abort = __syncthreads_or(abort ? 1 : 0);
+  if (tr && tid == 0) p.trace[3073] = clock64();
   // ---- merge the consumers' (m, l, O) per row in shared memory ----
 #pragma unroll
   for (int hr = 0; hr < 2 * MT; ++hr) {
@@ -472,6 +492,7 @@ int launch(const cf_attn_args &a, cudaStream_t stream) {
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = a.status;
   p.timeout_ns = a.timeout_ns ? a.timeout_ns : 2000000000ull;
+  p.trace = reinterpret_cast<unsigned long long *>(a.trace);
   if (p.nsplit > 1) {
     const size_t rows = (size_t)p.nsplit * p.B * p.Hkv * p.rows_total;
     const size_t need = rows * HD * sizeof(float) + rows * sizeof(float);

@@ -91,6 +91,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
   }
 }
 
+// Suspending variant: try_wait parks the thread in hardware until the phase
+// completes (or a hint expires) instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > limit_ns) return false;
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait_warp_sleep(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
+  return __all_sync(0xffffffffu, mbar_wait_sleep(bar, parity, limit_ns));
+}
+
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, limit_ns));
 }

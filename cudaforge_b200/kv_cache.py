@@ -149,7 +149,10 @@ class PagedKVCache:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:
-            _lib_kv().cf_kvcache_destroy(h)
+            try:
+                _lib_kv().cf_kvcache_destroy(h)
+            except Exception:  # interpreter shutdown: module globals may already be gone
+                pass
             self._h = None
 
     @staticmethod

@@ -300,6 +300,7 @@ typedef struct cf_attn_args {
   size_t workspace_bytes;
   int32_t *status;
   uint64_t timeout_ns;
+  uint64_t *trace;       /* optional profiling aid: [4][1024] SM-clock stamps of CTA 0 */
 } cf_attn_args;
 
 size_t cf_attention_workspace_bytes(const cf_attn_args *args);
