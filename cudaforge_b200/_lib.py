@@ -35,6 +35,18 @@ class CfAcceptArgs(ctypes.Structure):
     ]
 
 
+class CfAcceptTreeArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _I32), ("nodes", _I32), ("vocab", _I64), ("logits_dtype", _I32),
+        ("draft_logits", _P), ("draft_seq_stride", _I64), ("draft_row_stride", _I64),
+        ("target_logits", _P), ("target_seq_stride", _I64), ("target_row_stride", _I64),
+        ("parent", _P), ("tokens", _P), ("uniforms", _P), ("temperature", _F32),
+        ("eos_token_id", _I32), ("greedy", _I32),
+        ("out_path", _P), ("out_tokens", _P), ("out_num_accepted", _P), ("out_eos", _P),
+        ("workspace", _P), ("probs_draft", _P), ("probs_target", _P),
+    ]
+
+
 class CfGemmArgs(ctypes.Structure):
     _fields_ = [
         ("m", _I32), ("n", _I32), ("k", _I32), ("act_dtype", _I32),
@@ -97,6 +109,9 @@ def lib() -> ctypes.CDLL:
         L.cf_accept_workspace_bytes.restype = ctypes.c_size_t
         L.cf_accept_workspace_bytes.argtypes = [_I32, _I32]
         L.cf_accept_sample.argtypes = [ctypes.POINTER(CfAcceptArgs), _P]
+        L.cf_accept_tree_workspace_bytes.restype = ctypes.c_size_t
+        L.cf_accept_tree_workspace_bytes.argtypes = [_I32, _I32, _I64]
+        L.cf_accept_tree.argtypes = [ctypes.POINTER(CfAcceptTreeArgs), _P]
         L.cf_gemm_workspace_bytes.restype = ctypes.c_size_t
         L.cf_gemm_workspace_bytes.argtypes = [_I32, _I32, _I32, _I32, _I32]
         for fn in ("cf_w4a16_gemm", "cf_dense_gemm"):

@@ -127,3 +127,102 @@ def accept_sample(
         _lib.check(L.cf_accept_sample(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), "cf_accept_sample")
     _lib.count(3 if export_probs else 2)
     return out
+
+
+@dataclasses.dataclass
+class TreeAcceptResult:
+    """Per-sequence outcome of tree acceptance: path[b, :num_accepted[b]+1]
+    the accepted node ids (path[b, 0] = 0, the root), tokens[b,
+    :num_accepted[b]] their tokens and tokens[b, num_accepted[b]] the final
+    token."""
+
+    path: torch.Tensor          # [B, N+1] int32
+    tokens: torch.Tensor        # [B, N+1] int32
+    num_accepted: torch.Tensor  # [B] int32
+    eos: torch.Tensor           # [B] bool
+    probs_draft: Optional[torch.Tensor] = None   # [B, N+1, V] f32 (parity export)
+    probs_target: Optional[torch.Tensor] = None  # [B, N+1, V] f32 (parity export)
+
+    def emitted(self, b: int) -> list:
+        n = int(self.num_accepted[b])
+        return self.tokens[b, : n + 1].tolist()
+
+
+def accept_tree(
+    draft_logits: Optional[torch.Tensor],
+    target_logits: torch.Tensor,
+    parent: torch.Tensor,
+    tree_tokens: torch.Tensor,
+    uniforms: Optional[torch.Tensor] = None,
+    *,
+    temperature: float = 1.0,
+    eos_token_id: int = -1,
+    greedy: bool = False,
+    export_probs: bool = False,
+    workspace: Optional[torch.Tensor] = None,
+    stream: Optional[torch.cuda.Stream] = None,
+) -> TreeAcceptResult:
+    """Tree acceptance (cf_accept_tree).  The reference verifies chains only
+    (speculative.cpp:50-150); a tree whose every node has one child gives its
+    results exactly.  Node 0 is the root (last emitted token); parent[b, i] < i
+    for i > 0; siblings are tried in increasing node index.
+
+    draft_logits / target_logits [B, N+1, V]: row u is the distribution after
+    node u (draft: the one node u's children were drawn from).  parent and
+    tree_tokens [B, N+1] (entry 0 ignored), uniforms [B, N+1] fp32 (one per
+    acceptance test in walk order, then one for the final draw).
+    """
+    if target_logits.dim() != 3:
+        raise ValueError("target_logits must be [B, N+1, V]")
+    B, NN, V = target_logits.shape
+    dev = target_logits.device
+    if dev.type != "cuda":
+        raise ValueError("accept_tree runs on CUDA tensors only (no CPU fallback)")
+    if parent.shape != (B, NN) or tree_tokens.shape != (B, NN):
+        raise ValueError("parent and tree_tokens must be [B, N+1]")
+    if target_logits.dtype not in _DT:
+        raise ValueError(f"unsupported logits dtype {target_logits.dtype}")
+    if not greedy:
+        if draft_logits is None or draft_logits.shape != (B, NN, V):
+            raise ValueError("draft_logits [B, N+1, V] required for stochastic tree acceptance")
+        if draft_logits.dtype != target_logits.dtype or draft_logits.device != dev:
+            raise ValueError("draft and target logits must share dtype and device")
+        if uniforms is None or uniforms.shape != (B, NN):
+            raise ValueError("uniforms [B, N+1] required for stochastic acceptance")
+        uniforms = uniforms.to(device=dev, dtype=torch.float32).contiguous()
+    par = parent.to(device=dev, dtype=torch.int32).contiguous()
+    tk = tree_tokens.to(device=dev, dtype=torch.int32).contiguous()
+    ts, tr = _rows_view(target_logits, "target_logits")
+    ds, dr = _rows_view(draft_logits, "draft_logits") if draft_logits is not None else (0, V)
+    L = _lib.lib()
+    ws_bytes = L.cf_accept_tree_workspace_bytes(B, NN, V)
+    if workspace is None or workspace.numel() * workspace.element_size() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    out = TreeAcceptResult(
+        path=torch.full((B, NN), -1, dtype=torch.int32, device=dev),
+        tokens=torch.full((B, NN), -1, dtype=torch.int32, device=dev),
+        num_accepted=torch.zeros(B, dtype=torch.int32, device=dev),
+        eos=torch.zeros(B, dtype=torch.bool, device=dev),
+    )
+    if export_probs:
+        out.probs_draft = torch.empty((B, NN, V), dtype=torch.float32, device=dev) if draft_logits is not None else None
+        out.probs_target = torch.empty((B, NN, V), dtype=torch.float32, device=dev)
+    a = _lib.CfAcceptTreeArgs(
+        batch=B, nodes=NN, vocab=V, logits_dtype=_DT[target_logits.dtype],
+        draft_logits=draft_logits.data_ptr() if draft_logits is not None else None,
+        draft_seq_stride=ds, draft_row_stride=dr,
+        target_logits=target_logits.data_ptr(), target_seq_stride=ts, target_row_stride=tr,
+        parent=par.data_ptr(), tokens=tk.data_ptr(),
+        uniforms=uniforms.data_ptr() if not greedy else None,
+        temperature=float(temperature), eos_token_id=int(eos_token_id), greedy=int(bool(greedy)),
+        out_path=out.path.data_ptr(), out_tokens=out.tokens.data_ptr(),
+        out_num_accepted=out.num_accepted.data_ptr(), out_eos=out.eos.data_ptr(),
+        workspace=workspace.data_ptr(),
+        probs_draft=out.probs_draft.data_ptr() if out.probs_draft is not None else None,
+        probs_target=out.probs_target.data_ptr() if out.probs_target is not None else None,
+    )
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    with torch.cuda.device(dev):
+        _lib.check(L.cf_accept_tree(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), "cf_accept_tree")
+    _lib.count(3 if export_probs else 2)
+    return out

@@ -79,15 +79,15 @@ __device__ __forceinline__ void merge_stat(float &m, float &s, float m2, float s
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kStatsThreads)
-row_stats_kernel(cf_accept_args a, float c, RowStat *stats) {
+row_stats_kernel(cf_accept_args a, float c, RowStat *stats, int ndraft, int ntarget) {
   const int r = blockIdx.x, b = blockIdx.y;
-  const int rows = 2 * a.k + 1;
-  if (r < a.k && a.draft_logits == nullptr) {  // greedy without draft logits
+  const int rows = ndraft + ntarget;
+  if (r < ndraft && a.draft_logits == nullptr) {  // greedy without draft logits
     if (threadIdx.x == 0) stats[(int64_t)b * rows + r] = RowStat{-INFINITY, 0.0f};
     return;
   }
-  const T *x = (r < a.k) ? row_ptr<T>(a.draft_logits, a.draft_seq_stride, a.draft_row_stride, b, r)
-                         : row_ptr<T>(a.target_logits, a.target_seq_stride, a.target_row_stride, b, r - a.k);
+  const T *x = (r < ndraft) ? row_ptr<T>(a.draft_logits, a.draft_seq_stride, a.draft_row_stride, b, r)
+                            : row_ptr<T>(a.target_logits, a.target_seq_stride, a.target_row_stride, b, r - ndraft);
   const int64_t V = a.vocab;
   float m = -INFINITY, s = 0.0f;
   constexpr int N = cf::Vec16<T>::N;
@@ -153,15 +153,15 @@ row_stats_kernel(cf_accept_args a, float c, RowStat *stats) {
 // Optional parity export of the probabilities the decisions use.
 // ---------------------------------------------------------------------------
 template <typename T>
-__global__ void export_probs_kernel(cf_accept_args a, float c, const RowStat *stats) {
+__global__ void export_probs_kernel(cf_accept_args a, float c, const RowStat *stats, int ndraft, int ntarget) {
   const int r = blockIdx.x, b = blockIdx.y;
-  const int rows = 2 * a.k + 1;
-  const bool draft = r < a.k;
+  const int rows = ndraft + ntarget;
+  const bool draft = r < ndraft;
   if (draft ? (a.probs_draft == nullptr || a.draft_logits == nullptr) : a.probs_target == nullptr) return;
   const T *x = draft ? row_ptr<T>(a.draft_logits, a.draft_seq_stride, a.draft_row_stride, b, r)
-                     : row_ptr<T>(a.target_logits, a.target_seq_stride, a.target_row_stride, b, r - a.k);
-  float *out = draft ? a.probs_draft + ((int64_t)b * a.k + r) * a.vocab
-                     : a.probs_target + ((int64_t)b * (a.k + 1) + (r - a.k)) * a.vocab;
+                     : row_ptr<T>(a.target_logits, a.target_seq_stride, a.target_row_stride, b, r - ndraft);
+  float *out = draft ? a.probs_draft + ((int64_t)b * ndraft + r) * a.vocab
+                     : a.probs_target + ((int64_t)b * ntarget + (r - ndraft)) * a.vocab;
   const RowStat st = stats[(int64_t)b * rows + r];
   for (int64_t i = threadIdx.x; i < a.vocab; i += blockDim.x) out[i] = prob_of(cf::to_float(x[i]), c, st);
 }
@@ -536,18 +536,237 @@ decide_kernel(cf_accept_args a, float c, const RowStat *stats) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tree acceptance (no reference counterpart; a branching-1 tree reduces
+// exactly to the chain rule above).  Nodes 0..N, node 0 the root, parent[i] <
+// i, siblings tested in increasing node index.  Rows 0..N of the stats are
+// the draft rows (distribution each node's children were drawn from), rows
+// N+1..2N+1 the target rows.  The current distribution p is either a target
+// row (through its stats) or, after a rejected sibling, the normalised
+// residual held in this sequence's fp32 workspace row `resid`.
+// ---------------------------------------------------------------------------
+struct TreeArgs {
+  cf_accept_args a;  // batch, vocab, dtype, logits (row u = node u), uniforms, temperature, eos, greedy
+  int nodes;         // N + 1
+  const int32_t *parent, *tokens;
+  int32_t *out_path;
+  float *resid;      // [B][V]
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kDecideThreads)
+decide_tree_kernel(TreeArgs ta, float c, const RowStat *stats) {
+  __shared__ ScanShared sh;
+  __shared__ int s_cur, s_moved, s_any, s_used, s_resid, s_done, s_na;
+  __shared__ float s_r;
+  const cf_accept_args &a = ta.a;
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int NN = ta.nodes;
+  const int64_t V = a.vocab;
+  const RowStat *st = stats + (int64_t)b * 2 * NN;
+  const int32_t *par = ta.parent + (int64_t)b * NN;
+  const int32_t *tk = ta.tokens + (int64_t)b * NN;
+  const float *u = a.uniforms + (int64_t)b * NN;
+  int32_t *outt = a.out_tokens + (int64_t)b * NN;
+  int32_t *outp = ta.out_path + (int64_t)b * NN;
+  float *R = ta.resid + (int64_t)b * V;
+  if (tid == 0) { s_cur = 0; s_used = 0; s_resid = 0; s_done = 0; s_na = 0; outp[0] = 0; }
+  __syncthreads();
+  while (true) {
+    const int cur = s_cur;
+    const T *xt = row_ptr<T>(a.target_logits, a.target_seq_stride, a.target_row_stride, b, cur);
+    const RowStat stt = st[NN + cur];
+    if (a.greedy) {
+      const int64_t am = block_argmax<T>(xt, V, c, stt);
+      if (tid == 0) {
+        int moved = -1;
+        for (int ch = cur + 1; ch < NN; ++ch)
+          if (par[ch] == cur && tk[ch] == am) { moved = ch; break; }
+        if (moved < 0) {
+          outt[s_na] = (int32_t)am; a.out_num_accepted[b] = s_na; a.out_eos[b] = (am == a.eos_token_id); s_done = 1;
+        } else {
+          outp[++s_na] = moved; outt[s_na - 1] = tk[moved]; s_cur = moved;
+          if (tk[moved] == a.eos_token_id) { outt[s_na] = tk[moved]; a.out_num_accepted[b] = s_na; a.out_eos[b] = 1; s_done = 1; }
+        }
+      }
+      __syncthreads();
+      if (s_done) return;
+      continue;
+    }
+    const T *xd = row_ptr<T>(a.draft_logits, a.draft_seq_stride, a.draft_row_stride, b, cur);
+    const RowStat sdr = st[cur];
+    if (tid == 0) { s_moved = -1; s_any = 0; s_resid = 0; }
+    __syncthreads();
+    for (int ch = cur + 1; ch < NN; ++ch) {
+      if (par[ch] != cur) continue;  // uniform across the block
+      if (tid == 0) {
+        s_any = 1;
+        const int32_t x = tk[ch];
+        if (x < 0 || x >= V) { a.out_num_accepted[b] = -1; a.out_eos[b] = 0; s_done = 1; }
+        else {
+          const float qx = prob_of(cf::to_float(xd[x]), c, sdr);
+          const float px = s_resid ? R[x] : prob_of(cf::to_float(xt[x]), c, stt);
+          const float pq = __fdiv_rn(px, qx);
+          const float ratio = (qx > 0.0f) ? ((pq < 1.0f) ? pq : 1.0f) : 0.0f;
+          const float r = u[s_used++];
+          if (r <= ratio) s_moved = ch;
+        }
+      }
+      __syncthreads();
+      if (s_done) return;
+      if (s_moved >= 0) break;
+      // rejected: p <- norm(max(0, p - q)) unless that sum is <= 1e-6
+      const bool from_r = s_resid;
+      auto d8 = [&](int64_t i0, float (&o)[8]) {
+        float q8[8];
+        if (from_r) load8<float>(R, i0, V, o);
+        else {
+          load8<T>(xt, i0, V, o);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = prob_of(o[j], c, stt);
+        }
+        load8<T>(xd, i0, V, q8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float d = __fsub_rn(o[j], prob_of(q8[j], c, sdr));
+          o[j] = d > 0.0f ? d : 0.0f;
+        }
+      };
+      const float sum = exact_chain<false>(d8, V, 0.0f, nullptr, sh);
+      if (sum > 1e-6f) {
+        for (int64_t i0 = (int64_t)tid * 8; i0 < V; i0 += (int64_t)kDecideThreads * 8) {
+          float o[8];
+          d8(i0, o);  // reads the old R (if any) for exactly these elements before they are overwritten
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (i0 + j < V) R[i0 + j] = __fdiv_rn(o[j], sum);
+        }
+        __syncthreads();
+        if (tid == 0) s_resid = 1;
+        __syncthreads();
+      }
+    }
+    const int moved = s_moved;
+    if (moved >= 0) {
+      if (tid == 0) {
+        outp[++s_na] = moved;
+        outt[s_na - 1] = tk[moved];
+        s_cur = moved;
+        if (tk[moved] == a.eos_token_id) {
+          outt[s_na] = tk[moved]; a.out_num_accepted[b] = s_na; a.out_eos[b] = 1; s_done = 1;
+        }
+      }
+      __syncthreads();
+      if (s_done) return;
+      continue;
+    }
+    // all children rejected (draw from the current p) or a leaf (bonus from its target row)
+    if (tid == 0) s_r = u[s_used++];
+    __syncthreads();
+    const float r = s_r;
+    int64_t tok;
+    if (s_any && s_resid) {
+      auto r8 = [&](int64_t i0, float (&o)[8]) { load8<float>(R, i0, V, o); };
+      exact_chain<true>(r8, V, r, &tok, sh);
+    } else {
+      auto p8 = [&](int64_t i0, float (&o)[8]) {
+        load8<T>(xt, i0, V, o);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o[q] = prob_of(o[q], c, stt);
+      };
+      exact_chain<true>(p8, V, r, &tok, sh);
+    }
+    if (tid == 0) {
+      outt[s_na] = (int32_t)tok;
+      a.out_num_accepted[b] = s_na;
+      a.out_eos[b] = (tok == a.eos_token_id);
+    }
+    return;
+  }
+}
+
+template <typename T>
+int launch_accept_tree(const TreeArgs &ta, cudaStream_t stream) {
+  const cf_accept_args &a = ta.a;
+  const float c = (float)(1.4426950408889634 / (double)a.temperature);
+  RowStat *stats = reinterpret_cast<RowStat *>(a.workspace);
+  dim3 g1(2 * ta.nodes, a.batch);
+  row_stats_kernel<T><<<g1, kStatsThreads, 0, stream>>>(a, c, stats, ta.nodes, ta.nodes);
+  if (a.probs_draft || a.probs_target)
+    export_probs_kernel<T><<<g1, 256, 0, stream>>>(a, c, stats, ta.nodes, ta.nodes);
+  decide_tree_kernel<T><<<a.batch, kDecideThreads, 0, stream>>>(ta, c, stats);
+  return cf_launch_status();
+}
+
 template <typename T>
 int launch_accept(const cf_accept_args &a, cudaStream_t stream) {
   const float c = (float)(1.4426950408889634 / (double)a.temperature);
   RowStat *stats = reinterpret_cast<RowStat *>(a.workspace);
   dim3 g1(2 * a.k + 1, a.batch);
-  row_stats_kernel<T><<<g1, kStatsThreads, 0, stream>>>(a, c, stats);
-  if (a.probs_draft || a.probs_target) export_probs_kernel<T><<<g1, 256, 0, stream>>>(a, c, stats);
+  row_stats_kernel<T><<<g1, kStatsThreads, 0, stream>>>(a, c, stats, a.k, a.k + 1);
+  if (a.probs_draft || a.probs_target) export_probs_kernel<T><<<g1, 256, 0, stream>>>(a, c, stats, a.k, a.k + 1);
   decide_kernel<T><<<a.batch, kDecideThreads, 0, stream>>>(a, c, stats);
   return cf_launch_status();
 }
 
 }  // namespace
+
+static size_t tree_stats_bytes(int32_t batch, int32_t nodes) {
+  return ((size_t)batch * 2 * (size_t)nodes * sizeof(RowStat) + 255) & ~(size_t)255;
+}
+
+extern "C" size_t cf_accept_tree_workspace_bytes(int32_t batch, int32_t nodes, int64_t vocab) {
+  if (batch < 0 || nodes < 1 || vocab < 1) return 0;
+  return tree_stats_bytes(batch, nodes) + (size_t)batch * (size_t)vocab * sizeof(float);
+}
+
+extern "C" int cf_accept_tree(const cf_accept_tree_args *t, void *stream) {
+  if (!t) return CF_EINVAL;
+  cf_accept_args a{};
+  a.batch = t->batch;
+  a.k = 0;
+  a.vocab = t->vocab;
+  a.logits_dtype = t->logits_dtype;
+  a.draft_logits = t->draft_logits;
+  a.draft_seq_stride = t->draft_seq_stride;
+  a.draft_row_stride = t->draft_row_stride;
+  a.target_logits = t->target_logits;
+  a.target_seq_stride = t->target_seq_stride;
+  a.target_row_stride = t->target_row_stride;
+  a.uniforms = t->uniforms;
+  a.temperature = t->temperature;
+  a.eos_token_id = t->eos_token_id;
+  a.greedy = t->greedy;
+  a.out_tokens = t->out_tokens;
+  a.out_num_accepted = t->out_num_accepted;
+  a.out_eos = t->out_eos;
+  a.workspace = t->workspace;
+  a.probs_draft = t->probs_draft;
+  a.probs_target = t->probs_target;
+  if (a.batch < 0 || t->nodes < 1 || a.vocab < 1 || a.vocab > INT32_MAX || t->nodes > 65535 / 2) return CF_EINVAL;
+  if (a.batch == 0) return CF_OK;
+  if (!(a.temperature > 0.0f) || !isfinite(a.temperature)) return CF_EINVAL;
+  if (!a.target_logits || !t->parent || !t->tokens || !t->out_path || !a.out_tokens || !a.out_num_accepted ||
+      !a.out_eos || !a.workspace)
+    return CF_EINVAL;
+  if (!a.greedy && (!a.uniforms || !a.draft_logits)) return CF_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(a.workspace) & 255) != 0 || a.batch > 65535) return CF_EINVAL;
+  if (a.target_row_stride < a.vocab || (a.draft_logits && a.draft_row_stride < a.vocab)) return CF_EINVAL;
+  TreeArgs ta;
+  ta.a = a;
+  ta.nodes = t->nodes;
+  ta.parent = t->parent;
+  ta.tokens = t->tokens;
+  ta.out_path = t->out_path;
+  ta.resid = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(a.workspace) + tree_stats_bytes(a.batch, t->nodes));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (a.logits_dtype) {
+    case CF_F32: return launch_accept_tree<float>(ta, s);
+    case CF_BF16: return launch_accept_tree<__nv_bfloat16>(ta, s);
+    case CF_F16: return launch_accept_tree<__half>(ta, s);
+    default: return CF_EINVAL;
+  }
+}
 
 extern "C" size_t cf_accept_workspace_bytes(int32_t batch, int32_t k) {
   if (batch < 0 || k < 0) return 0;

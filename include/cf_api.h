@@ -128,6 +128,52 @@ int cf_accept_sample_noalloc(const cf_accept_args *args, void *stream);
 int cf_accept_noalloc_max_rows(void);
 
 /* ------------------------------------------------------------------------
+ * Tree acceptance.  The reference has no tree verifier; this extends
+ * verify_candidates (speculative.cpp:50-150) so that a branching-1 tree gives
+ * exactly its results.  Nodes 0..N (nodes = N+1): node 0 is the root (the
+ * last emitted token), parent[b][i] < i for i > 0, tokens[b][i] the draft
+ * token of node i; siblings are tried in increasing node index.  Logits row u
+ * of sequence b: target distribution after node u, and the draft
+ * distribution node u's children were drawn from (uses the strides of
+ * cf_accept_args).  Walking from the root with p = softmax(target[u] / T),
+ * q = softmax(draft[u] / T): each child is accepted iff
+ * uniforms[b][n] <= min(1, p[x]/q[x]) (q[x] > 0), n counting tests in order;
+ * a rejection replaces p with norm(max(0, p - q)) (kept when that sum is
+ * <= 1e-6) and tries the next sibling; when all children are rejected the
+ * final token is drawn from p, at a leaf from the leaf's target row; an
+ * accepted EOS stops.  Greedy: move to the child whose token is the argmax.
+ * Outputs: out_path[b][0..n] the accepted node ids (out_path[b][0] = 0),
+ * out_tokens[b][0..n] their tokens then the final token, n =
+ * out_num_accepted[b].  workspace: cf_accept_tree_workspace_bytes bytes,
+ * 256-B aligned (row statistics + one fp32 residual row per sequence).
+ * ---------------------------------------------------------------------- */
+typedef struct cf_accept_tree_args {
+  int32_t batch, nodes;
+  int64_t vocab;
+  int32_t logits_dtype;
+  const void *draft_logits;
+  int64_t draft_seq_stride, draft_row_stride;
+  const void *target_logits;
+  int64_t target_seq_stride, target_row_stride;
+  const int32_t *parent;   /* [B][nodes] */
+  const int32_t *tokens;   /* [B][nodes] */
+  const float *uniforms;   /* [B][nodes] */
+  float temperature;
+  int32_t eos_token_id;
+  int32_t greedy;
+  int32_t *out_path;       /* [B][nodes] */
+  int32_t *out_tokens;     /* [B][nodes] */
+  int32_t *out_num_accepted;
+  uint8_t *out_eos;
+  void *workspace;
+  float *probs_draft;      /* optional parity export [B][nodes][V] */
+  float *probs_target;     /* optional parity export [B][nodes][V] */
+} cf_accept_tree_args;
+
+size_t cf_accept_tree_workspace_bytes(int32_t batch, int32_t nodes, int64_t vocab);
+int cf_accept_tree(const cf_accept_tree_args *args, void *stream);
+
+/* ------------------------------------------------------------------------
  * GEMM on tcgen05 tensor cores (TMEM accumulators, TMA-staged operands)
  *
  * cf_w4a16_gemm replaces the reference INT4 GEMM launcher

@@ -88,6 +88,33 @@ def accept_greedy(draft_tokens, target_probs, eos):
     return tok, na, ef
 
 
+def accept_tree(parent, tokens, draft_probs, target_probs, uniforms, eos, greedy=False):
+    """Tree restatement for one sequence.  parent/tokens [N+1] (node 0 = root),
+    draft_probs / target_probs [N+1, V], uniforms [N+1].  Returns
+    (path [na+1], emitted tokens [na+1], na, eos)."""
+    par = np.ascontiguousarray(parent, dtype=np.int32)
+    tk = np.ascontiguousarray(tokens, dtype=np.int32)
+    tp = np.ascontiguousarray(target_probs, dtype=np.float32)
+    N = par.shape[0] - 1
+    V = tp.shape[-1]
+    path = np.full(N + 1, -1, np.int32)
+    out = np.full(N + 1, -1, np.int32)
+    na = np.zeros(1, np.int32)
+    ef = np.zeros(1, np.uint8)
+    if greedy:
+        lib().oref_accept_tree_greedy_one(ctypes.c_int32(N), ctypes.c_int64(V), _ptr(par), _ptr(tk), _ptr(tp),
+                                          ctypes.c_int32(eos), _ptr(path), _ptr(out), _ptr(na), _ptr(ef))
+    else:
+        dp = np.ascontiguousarray(draft_probs, dtype=np.float32)
+        u = np.ascontiguousarray(uniforms, dtype=np.float32)
+        rc = lib().oref_accept_tree_one(ctypes.c_int32(N), ctypes.c_int64(V), _ptr(par), _ptr(tk), _ptr(dp),
+                                        _ptr(tp), ctypes.c_int32(eos), _ptr(u), _ptr(path), _ptr(out),
+                                        _ptr(na), _ptr(ef))
+        assert rc == 0
+    n = int(na[0])
+    return path[: n + 1].tolist(), out[: n + 1].tolist(), n, int(ef[0])
+
+
 def softmax_rows(x: np.ndarray, T: float) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32)
     out = np.empty_like(x)

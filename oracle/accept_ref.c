@@ -202,3 +202,107 @@ void oref_softmax_row(const float *x, int64_t V, float T, float *p) {
   }
   for (int64_t i = 0; i < V; ++i) p[i] /= s;
 }
+
+/* ---------------------------------------------------------------------------
+ * Tree acceptance (no counterpart in the reference; defined by this build so
+ * that a branching-1 tree reduces exactly to oref_accept_one).
+ *
+ * Nodes 0..N: node 0 is the root (the last emitted token), node i > 0 has
+ * parent par[i] < i and token tok[i]; siblings are tested in increasing node
+ * index (the builder numbers them in draft-rank order).  target_probs[u] is
+ * the target distribution after node u, draft_probs[u] the draft
+ * distribution node u's children were drawn from.  Walk from the root with
+ * p = target_probs[u]:
+ *   for each child c: ratio = q[x_c] > 0 ? min(1, p[x_c] / q[x_c]) : 0,
+ *     accept iff u_next <= ratio  -> move to c (p = target_probs[c]);
+ *       an accepted EOS stops (final = EOS, no further draw);
+ *     reject -> d = max(0, p - q); s = sequential fp32 sum;
+ *       if s > 1e-6: p = d / s (element-wise)   (else p is kept)
+ *   all children rejected: final = sample_from(p, u_next)
+ *   leaf reached:          final = sample_from(target_probs[u], u_next)
+ * Outputs: path[0..na] = accepted node ids with path[0] = 0 (root), tokens of
+ * the accepted nodes then the final token, na accepted drafts, eos flag.
+ * ------------------------------------------------------------------------- */
+int oref_accept_tree_one(int32_t N, int64_t V, const int32_t *par, const int32_t *tok,
+                         const float *draft_probs,  /* [N+1][V] */
+                         const float *target_probs, /* [N+1][V] */
+                         int32_t eos, const float *u, int32_t *path, int32_t *tokens,
+                         int32_t *num_accepted, uint8_t *eos_flag) {
+  float *p = (float *)malloc(sizeof(float) * (size_t)(V > 0 ? V : 1));
+  float *d = (float *)malloc(sizeof(float) * (size_t)(V > 0 ? V : 1));
+  if (!p || !d) { free(p); free(d); return -1; }
+  int32_t cur = 0, na = 0, used = 0, final_tok = -1;
+  uint8_t e = 0;
+  path[0] = 0;
+  memcpy(p, target_probs, sizeof(float) * (size_t)V);
+  for (;;) {
+    const float *q = draft_probs + (size_t)cur * V;
+    int32_t moved = -1, any_child = 0;
+    for (int32_t c = cur + 1; c <= N; ++c) {
+      if (par[c] != cur) continue;
+      any_child = 1;
+      const int32_t x = tok[c];
+      const float qx = q[x], px = p[x];
+      const float pq = px / qx;
+      const float ratio = (qx > 0.0f) ? ((pq < 1.0f) ? pq : 1.0f) : 0.0f;
+      const float r = u[used++];
+      if (r <= ratio) { moved = c; break; }
+      float s = 0.0f;
+      for (int64_t i = 0; i < V; ++i) {
+        const float t = p[i] - q[i];
+        d[i] = t > 0.0f ? t : 0.0f;
+        s += d[i];
+      }
+      if (s > 1e-6f)
+        for (int64_t i = 0; i < V; ++i) p[i] = d[i] / s;
+    }
+    if (moved >= 0) {
+      cur = moved;
+      path[++na] = cur;
+      tokens[na - 1] = tok[cur];
+      if (tok[cur] == eos) { final_tok = eos; e = 1; break; }
+      memcpy(p, target_probs + (size_t)cur * V, sizeof(float) * (size_t)V);
+      continue;
+    }
+    final_tok = sample_from(any_child ? p : target_probs + (size_t)cur * V, V, u[used++]);
+    if (final_tok == eos) e = 1;
+    break;
+  }
+  tokens[na] = final_tok;
+  *num_accepted = na;
+  *eos_flag = e;
+  free(p);
+  free(d);
+  return 0;
+}
+
+/* Greedy tree: at node u move to the first child whose token equals the
+ * first-max argmax of target_probs[u]; otherwise final = that argmax (a leaf
+ * gives its own argmax as the bonus). */
+int oref_accept_tree_greedy_one(int32_t N, int64_t V, const int32_t *par, const int32_t *tok,
+                                const float *target_probs, int32_t eos, int32_t *path, int32_t *tokens,
+                                int32_t *num_accepted, uint8_t *eos_flag) {
+  int32_t cur = 0, na = 0;
+  path[0] = 0;
+  for (;;) {
+    const int32_t am = argmax_first(target_probs + (size_t)cur * V, V);
+    int32_t moved = -1;
+    for (int32_t c = cur + 1; c <= N; ++c)
+      if (par[c] == cur && tok[c] == am) { moved = c; break; }
+    if (moved < 0) {
+      tokens[na] = am;
+      *num_accepted = na;
+      *eos_flag = (am == eos);
+      return 0;
+    }
+    cur = moved;
+    path[++na] = cur;
+    tokens[na - 1] = tok[cur];
+    if (tok[cur] == eos) {
+      tokens[na] = eos;
+      *num_accepted = na;
+      *eos_flag = 1;
+      return 0;
+    }
+  }
+}

@@ -96,3 +96,26 @@ def test_cfg1_golden_vectors():
     res = g["uniforms_seed3_result"]
     assert na.tolist() == res["num_accepted"]
     assert [tok[b, : na[b] + 1].tolist() for b in range(c["B"])] == res["tokens"]
+
+
+def test_tree_restatement_branching_one_equals_chain():
+    """The tree walk (no reference counterpart) must reduce exactly to the
+    pinned chain restatement when every node has a single child."""
+    rng = np.random.default_rng(7)
+    for t in range(200):
+        K = int(rng.integers(0, 7))
+        V = int(rng.integers(2, 300))
+        dt, dp, tp = _case(rng, K, V, [0.0, 0.3, 1.0, 3.0][t % 4])
+        eos = int(dt[0]) if (t % 5 == 0 and K > 0) else -1
+        u = rng.random(K + 1).astype(np.float32)
+        tok, na, ef = oracle.accept(dt[None], dp[None], tp[None], u[None], eos)
+        par = np.maximum(np.arange(-1, K), 0).astype(np.int32)
+        ttok = np.concatenate([[0], dt]).astype(np.int32)
+        dp_tree = np.concatenate([dp, np.full((1, V), 1.0 / V, np.float32)]) if K else np.full((1, V), 1.0 / V, np.float32)
+        path, toks, n2, e2 = oracle.accept_tree(par, ttok, dp_tree, tp, u, eos)
+        assert n2 == na[0] and e2 == ef[0]
+        assert toks == tok[0, : na[0] + 1].tolist()
+        assert path == list(range(n2 + 1))
+        gtok, gna, gef = oracle.accept_greedy(dt[None], tp[None], eos)
+        path, toks, n2, e2 = oracle.accept_tree(par, ttok, None, tp, None, eos, greedy=True)
+        assert n2 == gna[0] and e2 == gef[0] and toks == gtok[0, : n2 + 1].tolist()
