@@ -263,25 +263,23 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       for (int i = 0; i < nkb; ++i) {
         const int sw = i % SW, sa = i % SA;
         if (!mbar_wait(&wfull[sw], (uint32_t)(i / SW) & 1u, p.timeout_ns)) { ok = false; break; }
-        if (i >= SA && !mbar_wait(&aempty[sa], ((uint32_t)(i / SA) & 1u) ^ 1u, p.timeout_ns)) { ok = false; break; }
-        tc_fence_after();
-        if (threadIdx.x == 64) CF_TRACE(1, i);
         const uint8_t *st = w_ring + sw * kWStageBytes;
         const uint32_t *wp = reinterpret_cast<const uint32_t *>(st);
         const __nv_bfloat16 sb =
             __float2bfloat16_rn(__half2float(reinterpret_cast<const __half *>(st + kWPackBytes)[t]));
         const __nv_bfloat162 s2 = __halves2bfloat162(sb, sb);
-        uint32_t w[8];
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) w[kk] = wp[kk * TN + t];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&wempty[sw]);  // packed words are in registers
         uint32_t a[32];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint4 v = dequant8(w[kk], s2);
+          const uint4 v = dequant8(wp[kk * TN + t], s2);
           a[4 * kk + 0] = v.x; a[4 * kk + 1] = v.y; a[4 * kk + 2] = v.z; a[4 * kk + 3] = v.w;
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wempty[sw]);  // packed words are consumed
+        // dequantised into registers first: only the TMEM store waits for the A slot
+        if (i >= SA && !mbar_wait(&aempty[sa], ((uint32_t)(i / SA) & 1u) ^ 1u, p.timeout_ns)) { ok = false; break; }
+        tc_fence_after();
+        if (threadIdx.x == 64) CF_TRACE(1, i);
         if (h < halves)
           tmem_st_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + p.a_tcol + (uint32_t)((sa * 2 + h) * 32), a);
         tmem_st_wait();
