@@ -112,6 +112,7 @@ def lib() -> ctypes.CDLL:
         L.cf_accept_tree_workspace_bytes.restype = ctypes.c_size_t
         L.cf_accept_tree_workspace_bytes.argtypes = [_I32, _I32, _I64]
         L.cf_accept_tree.argtypes = [ctypes.POINTER(CfAcceptTreeArgs), _P]
+        L.cf_topk_rows.argtypes = [_P, _I64, _I32, _I64, _I32, _I32, _P, _P, _P]
         L.cf_gemm_workspace_bytes.restype = ctypes.c_size_t
         L.cf_gemm_workspace_bytes.argtypes = [_I32, _I32, _I32, _I32, _I32]
         for fn in ("cf_w4a16_gemm", "cf_dense_gemm"):

@@ -173,6 +173,14 @@ typedef struct cf_accept_tree_args {
 size_t cf_accept_tree_workspace_bytes(int32_t batch, int32_t nodes, int64_t vocab);
 int cf_accept_tree(const cf_accept_tree_args *args, void *stream);
 
+/* Row-wise top-k of logits for the draft-tree builder (no reference
+ * counterpart; the reference drafts chains, cudaforge/speculative.py:113-123).
+ * rows x vocab logits (dtype CF_F32/CF_BF16/CF_F16) at row_stride elements;
+ * out_idx[rows][k] the k largest in descending order, ties to the lower index,
+ * NaN last (-1 when a row has fewer than k non-NaN entries); out_val optional. */
+int cf_topk_rows(const void *logits, int64_t row_stride, int32_t rows, int64_t vocab, int32_t dtype, int32_t k,
+                 int32_t *out_idx, float *out_val, void *stream);
+
 /* ------------------------------------------------------------------------
  * GEMM on tcgen05 tensor cores (TMEM accumulators, TMA-staged operands)
  *
