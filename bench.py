@@ -155,6 +155,40 @@ def setup(args, rank, device):
     return tcfg, target, cache, ver, draft_tokens.contiguous(), draft_logits.contiguous()
 
 
+def setup_tree(args, rank, device):
+    """cfg4: the 8B-INT4 target verifies a 64-node top-k tree (4/4/4, breadth-first
+    truncated) per sequence; the tree comes from the 1B draft (untimed)."""
+    from cudaforge_b200.model import DRAFT_1B, LLAMA_8B, LlamaModel
+    from cudaforge_b200.runner import PagedRunner
+    from cudaforge_b200.tree import TreeSpeculativeEngine, TreeVerifier, topk_tree_shape
+
+    tcfg, dcfg = LLAMA_8B, DRAFT_1B
+    B, P = args.batch, args.ctx
+    shape = topk_tree_shape((4, 4, 4), 64)
+    steps_total = args.warmup + 2 * args.steps + 4
+    blocks_per_seq = math.ceil((P + steps_total * 4) / 16) + 2
+    target = LlamaModel(tcfg, device=device, seed=1000 + rank)
+    cache = target.make_cache(B * blocks_per_seq + 8, max_batch=B, max_blocks_per_seq=blocks_per_seq + 4)
+    ver = TreeVerifier(target, cache, list(range(B)), shape, temperature=args.temperature,
+                       max_blocks_per_seq=blocks_per_seq + 4)
+    g = torch.Generator().manual_seed(7 + rank)
+    prompts = torch.randint(0, tcfg.vocab, (B, P), generator=g)
+    ver.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
+    gd = torch.Generator(device=device).manual_seed(11 + rank)
+    ver.fill_synthetic_kv(gd)
+    draft = LlamaModel(dcfg, device=device, seed=2000 + rank)
+    dcache = draft.make_cache(B * (math.ceil((P + 8) / 16) + 2) + 8, max_batch=B)
+    dr = PagedRunner(draft, dcache, list(range(B)))
+    dr.register(prompts[:, :-1].tolist())
+    for pool in (dcache.key_pool, dcache.value_pool):
+        pool.copy_(torch.randn(pool.shape, generator=gd, device=device).to(pool.dtype))
+    eng = TreeSpeculativeEngine(dr, dr, shape, temperature=args.temperature, seed=3 + rank)
+    ttok, tlog = eng.draft_tree(prompts.tolist())
+    del eng, dr, dcache, draft
+    torch.cuda.empty_cache()
+    return tcfg, target, cache, ver, ttok.contiguous(), tlog.contiguous()
+
+
 def run_ours(args):
     import torch.distributed as dist
 
@@ -168,8 +202,11 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    tcfg, target, cache, ver, dtok, dlog = setup(args, rank, device)
-    B, K, R = args.batch, args.k, args.k + 1
+    tree = args.config == "8b-tree"
+    tcfg, target, cache, ver, dtok, dlog = (setup_tree if tree else setup)(args, rank, device)
+    B = args.batch
+    R = dlog.shape[1] if tree else args.k + 1
+    K = R - 1
     total_steps = args.warmup + args.steps
     gen = torch.Generator(device=device).manual_seed(99 + rank)
     uni = torch.rand(total_steps + args.steps + 1, B, K + 1, generator=gen, device=device)
@@ -232,7 +269,7 @@ def run_ours(args):
     x1.record()
     barrier()
     e2e_ms = x0.elapsed_time(x1)
-    h2d = dtok.numel() * 4 + B * (K + 1) * 4
+    h2d = dtok.numel() * 4 + B * R * 4
     d2h = B * R * 4 + B * 4
 
     # max over ranks of the device times, sum of the emitted tokens (batch-sharded, no data-path collective)
@@ -272,9 +309,12 @@ def run_ours(args):
             "data": "synthetic: random-init weights (INT4 uniform [-8,7], |N(0,0.002)| fp16 scales), random "
                     "prompt ids, context K/V seeded random (stands in for a prefill), drafts from the random-init "
                     "1B INT4 draft model",
-            "config": {"workload": "cfg3 8B-INT4 verify+accept", "model": "Llama-3-8B-shaped W4A16 g128",
+            "config": {"workload": ("cfg4 8B-INT4 tree verify+accept (64-node top-k tree 4/4/4)" if tree
+                                    else "cfg3 8B-INT4 verify+accept"),
+                       "model": "Llama-3-8B-shaped W4A16 g128",
                        "draft": "1B-shaped W4A16 (excluded from timing)", "global_batch": B * world,
-                       "batch_per_gpu": B, "seq_len": args.ctx, "k": K, "temperature": args.temperature,
+                       "batch_per_gpu": B, "seq_len": args.ctx, **({"tree_nodes": K} if tree else {"k": K}),
+                       "temperature": args.temperature,
                        "parallelism": f"batch-sharded dp{world} (no collective)",
                        "l2": "inputs larger than L2 (3.9 GB weights + KV pools per GPU)",
                        "mean_accepted_per_seq_step": round(tok_all / (args.steps * B * world) - 1, 3)},
@@ -503,9 +543,10 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "tiny"])
-    ap.add_argument("--batch", type=int, default=64)
-    ap.add_argument("--ctx", type=int, default=1024)
+    ap.add_argument("--config", default="8b", choices=["8b", "tiny", "8b-tree"],
+                    help="8b = cfg3 chain (default); 8b-tree = cfg4 (B=32, 4096 context, 64-node tree)")
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--temperature", type=float, default=1.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -514,6 +555,10 @@ def main():
     ap.add_argument("--shape", default=None, help="NxK for --case gemm")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
+    if args.batch is None:
+        args.batch = 32 if args.config == "8b-tree" else 64
+    if args.ctx is None:
+        args.ctx = 4096 if args.config == "8b-tree" else 1024
     if args.case:
         run_case(args)
         return

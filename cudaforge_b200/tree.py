@@ -181,3 +181,74 @@ class TreeSpeculativeEngine:
         self.total_nodes += B * (N1 - 1)
         self.total_emitted += sum(len(e) for e in emitted)
         return TreeStepResult(emitted, res, tokens, (t1 - t0) * 1e3, (t2 - t1) * 1e3)
+
+
+class TreeVerifier:
+    """Device-resident tree verify + accept + commit for a fixed batch (the
+    tree counterpart of verifier.BatchVerifier, whose page-table and buffer
+    handling it reuses): one target forward over the N+1 tree nodes with the
+    ancestor mask, cf_accept_tree, then the accepted path's K/V rows committed
+    through cf_kv_commit's row map.  The only host round trip is the
+    num_accepted read-back the page tables need."""
+
+    def __init__(self, model, cache, seq_ids: Sequence[int], shape: Optional[TreeShape] = None, *,
+                 temperature: float = 1.0, greedy: bool = False, eos_token_id: int = -1,
+                 max_blocks_per_seq: int = 512):
+        from .verifier import BatchVerifier
+
+        self.shape = shape or topk_tree_shape()
+        N1 = self.shape.nodes
+        self.base = BatchVerifier(model, cache, seq_ids, N1 - 1, temperature=temperature, greedy=greedy,
+                                  eos_token_id=eos_token_id, max_blocks_per_seq=max_blocks_per_seq)
+        b = self.base
+        dev = model.device
+        self.depth = torch.tensor(self.shape.depth, dtype=torch.int32, device=dev).view(1, N1)
+        self.mask = self.shape.mask_words().to(dev).view(1, N1, -1).expand(b.B, N1, -1).contiguous()
+        self.parent = torch.tensor(self.shape.parent, dtype=torch.int32, device=dev).view(1, N1).expand(b.B, N1)
+        self.parent = self.parent.contiguous()
+        V = model.cfg.vocab
+        self.ws = torch.empty(_lib.lib().cf_accept_tree_workspace_bytes(b.B, N1, V) + 256, dtype=torch.uint8,
+                              device=dev)
+
+    def register_context(self, prompts, last_tokens) -> None:
+        self.base.register_context(prompts, last_tokens)
+
+    def fill_synthetic_kv(self, gen: torch.Generator, std: float = 1.0) -> None:
+        self.base.fill_synthetic_kv(gen, std)
+
+    @property
+    def ctx_host(self):
+        return self.base.ctx_host
+
+    @property
+    def n_pinned(self):
+        return self.base.n_pinned
+
+    @torch.no_grad()
+    def step(self, tree_tokens: torch.Tensor, draft_logits: Optional[torch.Tensor], uniforms: Optional[torch.Tensor],
+             timer=None) -> TreeAcceptResult:
+        """tree_tokens [B, N+1] int32 (column 0 ignored: the root is the last
+        emitted token), draft_logits [B, N+1, V], uniforms [B, N+1] fp32."""
+        b = self.base
+        B, N1 = b.B, b.R
+        b.tokens[:, 1:].copy_(tree_tokens[:, 1:])
+        torch.add(b.ctx.view(B, 1), self.depth, out=b.pos.view(B, N1))
+        logits = b.model.forward_rows(b.cache, b.tokens, b.pos, b.tables(), b.ctx, max(b.ctx_host),
+                                      tree_mask=self.mask, status=b.status, timer=timer)
+        res = accept_tree(None if b.greedy else draft_logits, logits.view(B, N1, -1), self.parent, b.tokens, uniforms,
+                          temperature=b.temperature, eos_token_id=b.eos, greedy=b.greedy, workspace=self.ws)
+        b.n_pinned.copy_(res.num_accepted, non_blocking=True)
+        torch.cuda.current_stream(b.model.device).synchronize()
+        n = [max(0, int(x)) + 1 for x in b.n_pinned.tolist()]
+        start = b.ctx.clone()
+        b.cache.append_batch(b.seq_ids, n)
+        b._upload_tables()
+        bf = b.model.buffers(B, N1)
+        from . import ops
+        ops.kv_commit(b.cache, bf["k_new"], bf["v_new"], res.num_accepted, start, b.tables(), n_commit_add=1,
+                      row_index=res.path, status=b.status)
+        b.ctx.add_(res.num_accepted.clamp_min(0) + 1)
+        b.ctx_host = [c + x for c, x in zip(b.ctx_host, n)]
+        idx = res.num_accepted.clamp_min(0).long().view(B, 1)
+        b.tokens[:, :1].copy_(res.tokens.gather(1, idx))
+        return res
