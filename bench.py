@@ -121,6 +121,15 @@ class KernelTimer:
         return len(self.ev.get(kind, []))
 
 
+def fill_random(cache, gen: torch.Generator) -> None:
+    """Seeded N(0,1) K/V in every pool slot, in chunks (no full-size fp32 temporary)."""
+    for pool in (cache.key_pool, cache.value_pool):
+        flat = pool.view(-1)
+        for i in range(0, flat.numel(), 1 << 28):
+            seg = flat[i: i + (1 << 28)]
+            seg.copy_(torch.randn(seg.numel(), generator=gen, device=seg.device).to(seg.dtype))
+
+
 def setup(args, rank, device):
     from cudaforge_b200.model import DRAFT_1B, LLAMA_8B, TINY_DRAFT, TINY_TARGET, LlamaModel
     from cudaforge_b200.runner import PagedRunner
@@ -145,9 +154,44 @@ def setup(args, rank, device):
     dcache = draft.make_cache(B * (math.ceil((P + K + 2) / 16) + 2) + 8, max_batch=B)
     dr = PagedRunner(draft, dcache, list(range(B)))
     dr.register(prompts[:, :-1].tolist())
-    for pool in (dcache.key_pool, dcache.value_pool):
-        pool.copy_(torch.randn(pool.shape, generator=gd, device=device).to(pool.dtype))
+    fill_random(dcache, gd)
     eng = SpeculativeEngine(dr, None, num_speculative_tokens=K, temperature=args.temperature, seed=3 + rank)
+    eng.target_runner = dr  # device lookup only
+    draft_tokens, draft_logits = eng.draft(prompts.tolist())
+    del dr, dcache, draft
+    torch.cuda.empty_cache()
+    return tcfg, target, cache, ver, draft_tokens.contiguous(), draft_logits.contiguous()
+
+
+def setup_tp(args, rank, world, device):
+    """cfg5: Llama-3-70B-shaped W4A16 target, tensor-parallel over the ranks
+    (TP = world size; 1 rank holds the whole model), B=128, 2048-token
+    contexts, K=4; drafts from an 8B-shaped INT4 draft replicated on every
+    rank (same seed everywhere, untimed)."""
+    from cudaforge_b200.model import LLAMA_8B, LLAMA_70B, LlamaModel, TensorParallel
+    from cudaforge_b200.runner import PagedRunner
+    from cudaforge_b200.speculative import SpeculativeEngine
+    from cudaforge_b200.verifier import BatchVerifier
+
+    tcfg, dcfg = LLAMA_70B, LLAMA_8B
+    B, P, K = args.batch, args.ctx, args.k
+    steps_total = args.warmup + 2 * args.steps + 4
+    blocks_per_seq = math.ceil((P + steps_total * (K + 1)) / 16) + 2
+    target = LlamaModel(tcfg, device=device, seed=1000, tp=TensorParallel(rank, world))
+    cache = target.make_cache(B * blocks_per_seq + 8, max_batch=B, max_blocks_per_seq=blocks_per_seq + 4)
+    ver = BatchVerifier(target, cache, list(range(B)), K, temperature=args.temperature,
+                        max_blocks_per_seq=blocks_per_seq + 4)
+    g = torch.Generator().manual_seed(7)
+    prompts = torch.randint(0, tcfg.vocab, (B, P), generator=g)
+    ver.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
+    gd = torch.Generator(device=device).manual_seed(11 + rank)
+    ver.fill_synthetic_kv(gd)
+    draft = LlamaModel(dcfg, device=device, seed=2000)
+    dcache = draft.make_cache(B * (math.ceil((P + K + 2) / 16) + 2) + 8, max_batch=B)
+    dr = PagedRunner(draft, dcache, list(range(B)))
+    dr.register(prompts[:, :-1].tolist())
+    fill_random(dcache, torch.Generator(device=device).manual_seed(13))
+    eng = SpeculativeEngine(dr, None, num_speculative_tokens=K, temperature=args.temperature, seed=3)
     eng.target_runner = dr  # device lookup only
     draft_tokens, draft_logits = eng.draft(prompts.tolist())
     del dr, dcache, draft
@@ -180,8 +224,7 @@ def setup_tree(args, rank, device):
     dcache = draft.make_cache(B * (math.ceil((P + 8) / 16) + 2) + 8, max_batch=B)
     dr = PagedRunner(draft, dcache, list(range(B)))
     dr.register(prompts[:, :-1].tolist())
-    for pool in (dcache.key_pool, dcache.value_pool):
-        pool.copy_(torch.randn(pool.shape, generator=gd, device=device).to(pool.dtype))
+    fill_random(dcache, gd)
     eng = TreeSpeculativeEngine(dr, dr, shape, temperature=args.temperature, seed=3 + rank)
     ttok, tlog = eng.draft_tree(prompts.tolist())
     del eng, dr, dcache, draft
@@ -203,7 +246,11 @@ def run_ours(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     tree = args.config == "8b-tree"
-    tcfg, target, cache, ver, dtok, dlog = (setup_tree if tree else setup)(args, rank, device)
+    tp = args.config == "70b-tp"
+    if tp:
+        tcfg, target, cache, ver, dtok, dlog = setup_tp(args, rank, world, device)
+    else:
+        tcfg, target, cache, ver, dtok, dlog = (setup_tree if tree else setup)(args, rank, device)
     B = args.batch
     R = dlog.shape[1] if tree else args.k + 1
     K = R - 1
@@ -276,13 +323,15 @@ def run_ours(args):
     from cudaforge_b200.shard import reduce_step_metrics
     (ms_max, e2e_max), (tok_all, e2e_tok_all) = reduce_step_metrics(
         [ms, e2e_ms], [float(sum(tokens_per_step)), float(e2e_tokens)], device=device)
+    if tp:  # every rank verifies the same batch: count its tokens once
+        tok_all, e2e_tok_all = tok_all / world, e2e_tok_all / world
     value = tok_all / (ms_max / 1e3)
     e2e_value = e2e_tok_all / (e2e_max / 1e3)
 
     # roofline of the dominant kernel (W4A16 GEMM, tensor bound) and the others
     peaks, peak_src = load_peaks()
     M = B * R
-    gemm_flops = tcfg.gemm_flops(M)
+    gemm_flops = tcfg.gemm_flops(M) / (world if tp else 1)  # per rank
     gemm_ms = kt.total_ms("gemm") / kp
     attn_ms = kt.total_ms("attn") / kp
     other_ms = kt.total_ms("other") / kp
@@ -290,7 +339,7 @@ def run_ours(args):
     achieved_tf = gemm_flops / (gemm_ms / 1e3) / 1e12
     peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     ctx_mean = statistics.mean(ver.ctx_host)
-    attn_bytes = tcfg.layers * B * (ctx_mean + R) * tcfg.n_kv_heads * tcfg.head_dim * 2 * 2
+    attn_bytes = tcfg.layers * B * (ctx_mean + R) * target.lcfg.n_kv_heads * tcfg.head_dim * 2 * 2  # per rank
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     traffic = None
     tr_path = os.path.join(ROOT, "profiles", "gemm_traffic.json")
@@ -305,24 +354,30 @@ def run_ours(args):
         out = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: random-init weights (INT4 uniform [-8,7], |N(0,0.002)| fp16 scales), random "
                     "prompt ids, context K/V seeded random (stands in for a prefill), drafts from the random-init "
                     "1B INT4 draft model",
             "config": {"workload": ("cfg4 8B-INT4 tree verify+accept (64-node top-k tree 4/4/4)" if tree
+                                    else f"cfg5 70B-INT4 TP-{world} verify+accept" if tp
                                     else "cfg3 8B-INT4 verify+accept"),
-                       "model": "Llama-3-8B-shaped W4A16 g128",
-                       "draft": "1B-shaped W4A16 (excluded from timing)", "global_batch": B * world,
+                       "model": "Llama-3-70B-shaped W4A16 g128" if tp else "Llama-3-8B-shaped W4A16 g128",
+                       "draft": ("8B-shaped W4A16 replicated per rank" if tp else "1B-shaped W4A16")
+                                + " (excluded from timing)",
+                       "global_batch": B if tp else B * world,
                        "batch_per_gpu": B, "seq_len": args.ctx, **({"tree_nodes": K} if tree else {"k": K}),
                        "temperature": args.temperature,
-                       "parallelism": f"batch-sharded dp{world} (no collective)",
-                       "l2": "inputs larger than L2 (3.9 GB weights + KV pools per GPU)",
-                       "mean_accepted_per_seq_step": round(tok_all / (args.steps * B * world) - 1, 3)},
+                       "parallelism": (f"tensor-parallel tp{world} (NCCL all-reduce after O and down, "
+                                       "all-gather of the vocabulary shards)" if tp
+                                       else f"batch-sharded dp{world} (no collective)"),
+                       "l2": "inputs larger than L2 (GB-sized INT4 weights + KV pools per GPU)",
+                       "mean_accepted_per_seq_step": round(tok_all / (args.steps * B * (1 if tp else world)) - 1, 3)},
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
             "clocks": clocks,
-            "roofline": {"bound": "tensor", "kernel": "w4a16_gemm (tcgen05, all 129 GEMMs of a step)",
+            "roofline": {"bound": "tensor", "kernel": f"w4a16_gemm (tcgen05, all {4 * tcfg.layers + 1} GEMMs of a step"
+                                   + (", per rank)" if tp else ")"),
                          "achieved": round(achieved_tf, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(achieved_tf / peak_tf, 4), "traffic": traffic,
                          "peak_source": f"{peak_src} bf16_tflops_sustained",
@@ -330,6 +385,7 @@ def run_ours(args):
             "kernels": {
                 "step_ms_instrumented": round(step_ms_k, 3),
                 "gemm_ms": round(gemm_ms, 3), "attn_ms": round(attn_ms, 3), "other_ms": round(other_ms, 3),
+                **({"comm_ms": round(kt.total_ms("comm") / kp, 3)} if tp else {}),
                 "attention": {"bound": "hbm", "bytes_per_step": attn_bytes,
                               "achieved_gbs": round(attn_bytes / (attn_ms / 1e3) / 1e9, 1),
                               "peak_gbs": hbm, "frac": round(attn_bytes / (attn_ms / 1e3) / 1e9 / hbm, 4)},
@@ -543,8 +599,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "tiny", "8b-tree"],
-                    help="8b = cfg3 chain (default); 8b-tree = cfg4 (B=32, 4096 context, 64-node tree)")
+    ap.add_argument("--config", default="8b", choices=["8b", "tiny", "8b-tree", "70b-tp"],
+                    help="8b = cfg3 chain (default); 8b-tree = cfg4 (B=32, 4096 context, 64-node tree); "
+                         "70b-tp = cfg5 (70B tensor-parallel over the ranks, B=128, 2048 context, K=4)")
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--k", type=int, default=5)
@@ -556,9 +613,11 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
     if args.batch is None:
-        args.batch = 32 if args.config == "8b-tree" else 64
+        args.batch = {"8b-tree": 32, "70b-tp": 128}.get(args.config, 64)
     if args.ctx is None:
-        args.ctx = 4096 if args.config == "8b-tree" else 1024
+        args.ctx = {"8b-tree": 4096, "70b-tp": 2048}.get(args.config, 1024)
+    if args.config == "70b-tp" and args.k == 5:
+        args.k = 4
     if args.case:
         run_case(args)
         return

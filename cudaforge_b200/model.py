@@ -78,10 +78,98 @@ class Linear:
         else:
             self.w = (torch.randn(n, k, generator=gen, device=device) * std).to(cfg.dtype)
 
+    @classmethod
+    def _wrap(cls, quant, n, k, wq=None, scales=None, w=None):
+        lin = cls.__new__(cls)
+        lin.n, lin.k, lin.quant = n, k, quant
+        if quant == "int4":
+            lin.wq, lin.scales = wq.contiguous(), scales.contiguous()
+        else:
+            lin.w = w.contiguous()
+        return lin
+
+    def take_columns(self, cols: torch.Tensor, pad_to: int = 0) -> "Linear":
+        """Column-parallel shard: output features `cols` (zero columns appended
+        up to pad_to, for the GEMM's 128-wide N tiles)."""
+        n = max(int(cols.numel()), pad_to)
+        if self.quant == "int4":
+            wq, sc = self.wq[:, cols], self.scales[:, cols]
+            if n > cols.numel():  # nibble 8 is zero; scale 0 makes the padded outputs exactly 0
+                wq = torch.cat([wq, torch.full((wq.shape[0], n - cols.numel()), -2004318072, dtype=wq.dtype,
+                                                device=wq.device)], 1)
+                sc = torch.cat([sc, torch.zeros((sc.shape[0], n - cols.numel()), dtype=sc.dtype, device=sc.device)], 1)
+            return Linear._wrap("int4", n, self.k, wq=wq, scales=sc)
+        w = self.w[cols]
+        if n > cols.numel():
+            w = torch.cat([w, torch.zeros((n - cols.numel(), self.k), dtype=w.dtype, device=w.device)], 0)
+        return Linear._wrap(self.quant, n, self.k, w=w)
+
+    def take_rows(self, k0: int, k1: int) -> "Linear":
+        """Row-parallel shard: input features [k0, k1) (multiples of 128)."""
+        if self.quant == "int4":
+            return Linear._wrap("int4", self.n, k1 - k0, wq=self.wq[k0 // 8: k1 // 8], scales=self.scales[k0 // 128: k1 // 128])
+        return Linear._wrap(self.quant, self.n, k1 - k0, w=self.w[:, k0:k1])
+
     def __call__(self, x, out=None, residual=None, workspace=None):
         if self.quant == "int4":
             return w4a16_gemm(x, self.wq, self.scales, out=out, residual=residual, workspace=workspace)
         return dense_gemm(x, self.w, out=out, residual=residual, workspace=workspace)
+
+
+@dataclasses.dataclass(frozen=True)
+class TensorParallel:
+    """Megatron-style tensor parallelism over `size` ranks (one process per
+    GPU, NCCL): QKV and gate|up column-parallel (heads / FFN features split),
+    O and down row-parallel with an all-reduce of the residual stream after
+    each, lm_head column-parallel over the vocabulary with an all-gather of
+    the logits (acceptance then runs on the full rows, identically on every
+    rank).  `group` is a torch.distributed process group (None = default)."""
+
+    rank: int
+    size: int
+    group: object = None
+
+
+def tp_local_config(cfg: LlamaConfig, size: int) -> LlamaConfig:
+    """The per-rank shapes of a `size`-way tensor-parallel model."""
+    if size == 1:
+        return cfg
+    if cfg.n_heads % size or cfg.n_kv_heads % size or cfg.ffn % size or cfg.vocab % size:
+        raise ValueError(f"{cfg} does not split {size} ways")
+    if (cfg.n_heads // size) * cfg.head_dim % 128 or (cfg.ffn // size) % 128:
+        raise ValueError("row-parallel K shards must be multiples of 128 (INT4 groups / GEMM tiles)")
+    return dataclasses.replace(cfg, n_heads=cfg.n_heads // size, n_kv_heads=cfg.n_kv_heads // size,
+                               ffn=cfg.ffn // size, vocab=cfg.vocab // size)
+
+
+def tp_columns(cfg: LlamaConfig, name: str, rank: int, size: int, device) -> torch.Tensor:
+    """Output-feature indices of rank `rank`'s column-parallel shard."""
+    D = cfg.head_dim
+    ar = lambda a, b: torch.arange(a, b, device=device)  # noqa: E731
+    if name == "qkv":
+        hq, hk = cfg.n_heads // size, cfg.n_kv_heads // size
+        q0, k0, v0 = 0, cfg.n_heads * D, (cfg.n_heads + cfg.n_kv_heads) * D
+        return torch.cat([ar(q0 + rank * hq * D, q0 + (rank + 1) * hq * D),
+                          ar(k0 + rank * hk * D, k0 + (rank + 1) * hk * D),
+                          ar(v0 + rank * hk * D, v0 + (rank + 1) * hk * D)])
+    if name == "gate_up":
+        f = cfg.ffn // size
+        return torch.cat([ar(rank * f, (rank + 1) * f), ar(cfg.ffn + rank * f, cfg.ffn + (rank + 1) * f)])
+    if name == "lm_head":
+        v = cfg.vocab // size
+        return ar(rank * v, (rank + 1) * v)
+    raise KeyError(name)
+
+
+def tp_rows(cfg: LlamaConfig, name: str, rank: int, size: int):
+    """Input-feature range [k0, k1) of rank `rank`'s row-parallel shard."""
+    if name == "o":
+        w = cfg.n_heads // size * cfg.head_dim
+    elif name == "down":
+        w = cfg.ffn // size
+    else:
+        raise KeyError(name)
+    return rank * w, (rank + 1) * w
 
 
 class _NullCtx:
@@ -99,8 +187,13 @@ def _null_timer(kind):
 class LlamaModel:
     """Random-init Llama-shaped model (seeded), resident on one device."""
 
-    def __init__(self, cfg: LlamaConfig, device="cuda", seed: int = 0):
+    def __init__(self, cfg: LlamaConfig, device="cuda", seed: int = 0, tp: Optional[TensorParallel] = None):
+        """With `tp`, every rank draws the full model from the same seeded
+        stream (so a TP model equals the single-GPU model of that seed) and
+        keeps its shards; `cfg` stays the global shape, `lcfg` is per rank."""
         self.cfg = cfg
+        self.tp = tp if (tp is not None and tp.size > 1) else None
+        self.lcfg = tp_local_config(cfg, self.tp.size) if self.tp else cfg
         self.device = torch.device(device)
         g = torch.Generator(device=self.device).manual_seed(seed)
         dt = cfg.dtype
@@ -112,17 +205,31 @@ class LlamaModel:
                 "ffn_norm": (torch.randn(cfg.d_model, generator=g, device=self.device) * 0.02 + 1.0).to(dt),
             }
             for name, n, k in cfg.linear_shapes():
-                lay[name] = Linear(n, k, cfg, g, self.device)
+                lay[name] = self._shard(name, Linear(n, k, cfg, g, self.device))
             self.layers.append(lay)
         self.final_norm = (torch.randn(cfg.d_model, generator=g, device=self.device) * 0.02 + 1.0).to(dt)
-        self.lm_head = Linear(cfg.vocab, cfg.d_model, cfg, g, self.device)
+        self.lm_head = self._shard("lm_head", Linear(cfg.vocab, cfg.d_model, cfg, g, self.device))
         self._bufs = {}
+
+    def _shard(self, name: str, lin: Linear) -> Linear:
+        if self.tp is None:
+            return lin
+        r, n = self.tp.rank, self.tp.size
+        if name in ("o", "down"):
+            return lin.take_rows(*tp_rows(self.cfg, name, r, n))
+        cols = tp_columns(self.cfg, name, r, n, lin.wq.device if lin.quant == "int4" else lin.w.device)
+        pad = ((cols.numel() + 127) // 128) * 128 if name == "lm_head" else 0
+        return lin.take_columns(cols, pad_to=pad)
+
+    def _all_reduce(self, x: torch.Tensor) -> None:
+        import torch.distributed as dist
+        dist.all_reduce(x, group=self.tp.group)
 
     # ---- scratch buffers, sized once per (B, R) and reused (graph friendly) ----
     def buffers(self, B: int, R: int):
         key = (B, R)
         if key not in self._bufs:
-            c, M, dev, dt = self.cfg, B * R, self.device, self.cfg.dtype
+            c, M, dev, dt = self.lcfg, B * R, self.device, self.cfg.dtype
             self._bufs[key] = {
                 "h": torch.empty(M, c.d_model, dtype=dt, device=dev),
                 "xn": torch.empty(M, c.d_model, dtype=dt, device=dev),
@@ -130,10 +237,14 @@ class LlamaModel:
                 "attn": torch.empty(M, c.n_heads * c.head_dim, dtype=dt, device=dev),
                 "gu": torch.empty(M, 2 * c.ffn, dtype=dt, device=dev),
                 "act": torch.empty(M, c.ffn, dtype=dt, device=dev),
-                "logits": torch.empty(M, c.vocab, dtype=dt, device=dev),
+                "logits": torch.empty(M, self.cfg.vocab, dtype=dt, device=dev),
                 "k_new": torch.empty(c.layers, B, R, c.n_kv_heads, c.head_dim, dtype=dt, device=dev),
                 "v_new": torch.empty(c.layers, B, R, c.n_kv_heads, c.head_dim, dtype=dt, device=dev),
             }
+            if self.tp is not None:
+                n = self.lm_head.n
+                self._bufs[key]["logits_local"] = torch.empty(M, n, dtype=dt, device=dev)
+                self._bufs[key]["logits_gather"] = torch.empty(self.tp.size, M, n, dtype=dt, device=dev)
         return self._bufs[key]
 
     def forward_rows(self, cache, tokens: torch.Tensor, positions: torch.Tensor, block_tables: torch.Tensor,
@@ -145,7 +256,8 @@ class LlamaModel:
         (a reused buffer) and leaves this step's K/V rows in buffers()["k_new"/"v_new"].
         `timer(kind)` (optional) returns a context manager wrapped around each
         launch group ("gemm", "attn", "other") for per-kernel timing."""
-        c = self.cfg
+        c = self.lcfg
+        tp = self.tp
         B, R = tokens.shape
         bf = self.buffers(B, R)
         h, xn, qkv, attn, gu, act = bf["h"], bf["xn"], bf["qkv"], bf["attn"], bf["gu"], bf["act"]
@@ -164,8 +276,11 @@ class LlamaModel:
                 ops.verify_attention(cache, li, qkv, bf["k_new"][li], bf["v_new"][li], block_tables, context_lens,
                                      max_context, rows=R, num_q_heads=c.n_heads, out=attn, tree_mask=tree_mask,
                                      status=status)
-            with T("gemm"):
-                lay["o"](attn, out=h, residual=h)
+            with T("gemm"):  # TP: rank 0 carries the residual, the all-reduce sums the partial outputs
+                lay["o"](attn, out=h, residual=h if tp is None or tp.rank == 0 else None)
+            if tp is not None:
+                with T("comm"):
+                    self._all_reduce(h)
             with T("other"):
                 ops.rmsnorm(h, lay["ffn_norm"], c.eps, out=xn)
             with T("gemm"):
@@ -173,17 +288,29 @@ class LlamaModel:
             with T("other"):
                 ops.silu_mul(gu, c.ffn, out=act)
             with T("gemm"):
-                lay["down"](act, out=h, residual=h)
+                lay["down"](act, out=h, residual=h if tp is None or tp.rank == 0 else None)
+            if tp is not None:
+                with T("comm"):
+                    self._all_reduce(h)
         with T("other"):
             ops.rmsnorm(h, self.final_norm, c.eps, out=xn)
+        if tp is None:
+            with T("gemm"):
+                self.lm_head(xn, out=bf["logits"])
+            return bf["logits"]
+        import torch.distributed as dist
         with T("gemm"):
-            self.lm_head(xn, out=bf["logits"])
+            self.lm_head(xn, out=bf["logits_local"])
+        with T("comm"):
+            dist.all_gather_into_tensor(bf["logits_gather"], bf["logits_local"], group=tp.group)
+            v = c.vocab  # this rank's true vocabulary slice (the shard is padded to 128 columns)
+            bf["logits"].view(-1, tp.size, v).copy_(bf["logits_gather"][:, :, :v].permute(1, 0, 2))
         return bf["logits"]
 
     def make_cache(self, total_blocks: int, max_batch: int = 256, max_blocks_per_seq: int = 512,
                    prefix_caching: bool = False):
         from .kv_cache import KVCacheConfig, PagedKVCache
-        c = self.cfg
+        c = self.lcfg
         kc = KVCacheConfig(num_layers=c.layers, num_kv_heads=c.n_kv_heads, head_dim=c.head_dim, block_size=16,
                            element_size_bytes=2, total_gpu_blocks=total_blocks,
                            enable_prefix_caching=prefix_caching, max_supported_batch_size=max_batch,
