@@ -143,7 +143,7 @@ def setup(args, rank, device):
     target = LlamaModel(tcfg, device=device, seed=1000 + rank)
     cache = target.make_cache(B * blocks_per_seq + 8, max_batch=B, max_blocks_per_seq=blocks_per_seq + 4)
     ver = BatchVerifier(target, cache, list(range(B)), K, temperature=args.temperature,
-                        max_blocks_per_seq=blocks_per_seq + 4)
+                        max_blocks_per_seq=blocks_per_seq + 4, use_graph=not args.no_graph)
     g = torch.Generator().manual_seed(7 + rank)
     prompts = torch.randint(0, tcfg.vocab, (B, P), generator=g)
     ver.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
@@ -607,6 +607,7 @@ def main():
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--temperature", type=float, default=1.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch every kernel eagerly (no CUDA graphs)")
     ap.add_argument("--case", default=None, choices=["gemm", "attention", "accept"],
                     help="time a single kernel at the bench shapes (profiling aid)")
     ap.add_argument("--shape", default=None, help="NxK for --case gemm")

@@ -14,7 +14,11 @@ reference's native acceptance semantics, speculative.cpp:50-103):
 
 All per-step state (token rows, positions, context lengths, block tables,
 acceptance outputs) lives in preallocated device buffers; the only host
-round trip is the num_accepted read-back the page tables need.
+round trip is the num_accepted read-back the page tables need.  With
+`use_graph=True` the step runs as two CUDA graphs (verify forward +
+acceptance; KV commit + state update) captured on the second call, around
+that read-back and the page-table upload; block tables therefore have a
+fixed width (max_blocks_per_seq) on the device.
 """
 from __future__ import annotations
 
@@ -29,7 +33,8 @@ from .model import LlamaModel
 
 class BatchVerifier:
     def __init__(self, model: LlamaModel, cache, seq_ids: Sequence[int], k: int, *, temperature: float = 1.0,
-                 greedy: bool = False, eos_token_id: int = -1, max_blocks_per_seq: int = 512):
+                 greedy: bool = False, eos_token_id: int = -1, max_blocks_per_seq: int = 512,
+                 use_graph: bool = False):
         self.model, self.cache = model, cache
         self.seq_ids = list(seq_ids)
         self.B, self.K, self.R = len(self.seq_ids), k, k + 1
@@ -43,7 +48,9 @@ class BatchVerifier:
         self.ar = torch.arange(R, dtype=torch.int32, device=dev).view(1, R)
         self.tables_pinned = torch.full((B * max_blocks_per_seq,), -1, dtype=torch.int32).pin_memory()
         self.ctx_pinned = torch.zeros(B, dtype=torch.int32).pin_memory()
-        self.tables_dev = torch.full((B * max_blocks_per_seq,), -1, dtype=torch.int32, device=dev)
+        self.cap = max_blocks_per_seq
+        self.tables_fixed = torch.full((B, max_blocks_per_seq), -1, dtype=torch.int32).pin_memory()
+        self.tables_dev = torch.full((B, max_blocks_per_seq), -1, dtype=torch.int32, device=dev)
         self.max_blocks = 0
         self.n_pinned = torch.zeros(B, dtype=torch.int32).pin_memory()
         self.res = AcceptResult(tokens=torch.zeros(B, R, dtype=torch.int32, device=dev),
@@ -52,15 +59,26 @@ class BatchVerifier:
         self.ws = torch.empty(4096 + 16 * B * (2 * k + 1), dtype=torch.uint8, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.model.buffers(B, R)
+        # CUDA graphs (single-GPU models only: the TP collectives stay eager)
+        self.use_graph = use_graph and getattr(model, "tp", None) is None
+        self.graphs = None
+        self.g_in = None          # static inputs of the captured forward: (draft tokens, draft logits, uniforms)
+        self.start = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.kernels_per_step = 0
+        self._keep = []
 
     # ---- state ----
     def _upload_tables(self, stream=None):
-        self.max_blocks = self.cache.prepare_batch_into(self.seq_ids, self.tables_pinned, self.ctx_pinned)
-        n = self.B * self.max_blocks
-        self.tables_dev[:n].copy_(self.tables_pinned[:n], non_blocking=True)
+        mb = self.cache.prepare_batch_into(self.seq_ids, self.tables_pinned, self.ctx_pinned)
+        if mb > self.cap:
+            raise ValueError(f"a sequence needs {mb} blocks > max_blocks_per_seq={self.cap}")
+        self.max_blocks = mb
+        # fixed-width device tables (-1 past each row's blocks): the captured graphs keep one stride
+        self.tables_fixed[:, :mb].copy_(self.tables_pinned[: self.B * mb].view(self.B, mb))
+        self.tables_dev.copy_(self.tables_fixed, non_blocking=True)
 
     def tables(self) -> torch.Tensor:
-        return self.tables_dev[: self.B * self.max_blocks].view(self.B, self.max_blocks)
+        return self.tables_dev
 
     def register_context(self, prompts, last_tokens) -> None:
         """Register each sequence's cached prompt (page tables) and set row 0
@@ -84,31 +102,79 @@ class BatchVerifier:
                 seg.copy_((torch.randn(seg.numel(), generator=gen, device=seg.device) * std).to(seg.dtype))
 
     # ---- the step ----
+    def _forward_accept(self, draft_tokens, draft_logits, uniforms, timer=None, max_context=None) -> AcceptResult:
+        B, R = self.B, self.R
+        self.tokens[:, 1:].copy_(draft_tokens)
+        torch.add(self.ctx.view(B, 1), self.ar, out=self.pos.view(B, R))
+        logits = self.model.forward_rows(self.cache, self.tokens, self.pos, self.tables(), self.ctx,
+                                         max_context if max_context is not None else max(self.ctx_host),
+                                         status=self.status, timer=timer)
+        return accept_sample(draft_logits, logits.view(B, R, -1), draft_tokens, uniforms,
+                             temperature=self.temperature, eos_token_id=self.eos, greedy=self.greedy,
+                             workspace=self.ws, out=self.res)
+
+    def _commit_update(self, res: AcceptResult) -> None:
+        B, R = self.B, self.R
+        bf = self.model.buffers(B, R)
+        self.start.copy_(self.ctx)
+        ops.kv_commit(self.cache, bf["k_new"], bf["v_new"], res.num_accepted, self.start, self.tables(),
+                      n_commit_add=1, status=self.status)
+        # next round: context grows by n, row 0 = the final token
+        self.ctx.add_(res.num_accepted.clamp_min(0) + 1)
+        idx = res.num_accepted.clamp_min(0).long().view(B, 1)
+        self.tokens[:, :1].copy_(res.tokens.gather(1, idx))
+
+    def _capture(self, draft_tokens, draft_logits, uniforms) -> None:
+        from . import gemm as _gemm
+        # hold every workspace the captured kernels address (the caches may grow later)
+        self._keep = [dict(ops._Ws.bufs), dict(_gemm._Ws.bufs)]
+        g_tok = draft_tokens.to(dtype=torch.int32).clone()
+        g_uni = None if uniforms is None else uniforms.clone()
+        self.g_in = (g_tok, draft_logits, g_uni)  # draft logits are captured by address
+        max_ctx = self.cap * self.cache.get_config().block_size
+        g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            self._forward_accept(g_tok, draft_logits, g_uni, max_context=max_ctx)
+        with torch.cuda.graph(g2):
+            self._commit_update(self.res)
+        self.graphs = (g1, g2)
+
     @torch.no_grad()
     def step(self, draft_tokens: torch.Tensor, draft_logits: Optional[torch.Tensor],
              uniforms: Optional[torch.Tensor], timer=None) -> AcceptResult:
         """draft_tokens [B, K] int32 and draft_logits [B, K, V] (device),
         uniforms [B, K+1] fp32 (device; unused when greedy).  Returns the
-        acceptance result (device tensors, reused across steps)."""
-        B, R = self.B, self.R
-        self.tokens[:, 1:].copy_(draft_tokens)
-        torch.add(self.ctx.view(B, 1), self.ar, out=self.pos.view(B, R))
-        logits = self.model.forward_rows(self.cache, self.tokens, self.pos, self.tables(), self.ctx,
-                                         max(self.ctx_host), status=self.status, timer=timer)
-        res = accept_sample(draft_logits, logits.view(B, R, -1), draft_tokens, uniforms,
-                            temperature=self.temperature, eos_token_id=self.eos, greedy=self.greedy,
-                            workspace=self.ws, out=self.res)
+        acceptance result (device tensors, reused across steps).  In graph
+        mode the captured forward reads the draft logits at the address seen
+        at capture; a different tensor is copied there first."""
+        from . import _lib
+        graph = self.use_graph and timer is None
+        l0 = _lib.LAUNCHES[0]
+        if graph and self.graphs is None and self.kernels_per_step:
+            self._capture(draft_tokens, draft_logits, uniforms)
+            _lib.LAUNCHES[0] = l0  # capture records launches without running them
+        if graph and self.graphs is not None:
+            g_tok, g_dlog, g_uni = self.g_in
+            g_tok.copy_(draft_tokens)
+            if g_uni is not None:
+                g_uni.copy_(uniforms)
+            if draft_logits is not None and draft_logits.data_ptr() != g_dlog.data_ptr():
+                g_dlog.copy_(draft_logits)
+            self.graphs[0].replay()
+            res = self.res
+        else:
+            res = self._forward_accept(draft_tokens, draft_logits, uniforms, timer=timer)
         self.n_pinned.copy_(res.num_accepted, non_blocking=True)
         torch.cuda.current_stream(self.model.device).synchronize()
         n = [max(0, int(x)) + 1 for x in self.n_pinned.tolist()]
-        start = self.ctx.clone()
         self.cache.append_batch(self.seq_ids, n)
         self._upload_tables()
-        ops.kv_commit(self.cache, self.model.buffers(B, R)["k_new"], self.model.buffers(B, R)["v_new"],
-                      res.num_accepted, start, self.tables(), n_commit_add=1, status=self.status)
-        # next round: context grows by n, row 0 = the final token
-        self.ctx.add_(res.num_accepted.clamp_min(0) + 1)
+        if graph and self.graphs is not None:
+            self.graphs[1].replay()
+            _lib.count(self.kernels_per_step)
+        else:
+            self._commit_update(res)
+            if not self.kernels_per_step:
+                self.kernels_per_step = _lib.LAUNCHES[0] - l0
         self.ctx_host = [c + x for c, x in zip(self.ctx_host, n)]
-        idx = res.num_accepted.clamp_min(0).long().view(B, 1)
-        self.tokens[:, :1].copy_(res.tokens.gather(1, idx))
         return res
