@@ -341,13 +341,13 @@ def run_ours(args):
     ctx_mean = statistics.mean(ver.ctx_host)
     attn_bytes = tcfg.layers * B * (ctx_mean + R) * target.lcfg.n_kv_heads * tcfg.head_dim * 2 * 2  # per rank
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    # DRAM bytes of the step's GEMMs from the committed ncu summary (cfg3 shapes only)
     traffic = None
-    tr_path = os.path.join(ROOT, "profiles", "gemm_traffic.json")
-    if os.path.exists(tr_path):
-        try:
-            traffic = json.load(open(tr_path)).get("traffic_bytes_per_step")
-        except (OSError, ValueError):
-            traffic = None
+    tr_path = os.path.join(ROOT, "profiles", "w4a16_gemm_traffic_cfg3.md")
+    if not tree and not tp and B == 64 and K == 5 and os.path.exists(tr_path):
+        import re
+        m = re.search(r"traffic_bytes_per_step:\s*(\d+)", open(tr_path).read())
+        traffic = int(m.group(1)) if m else None
 
     out = None
     if rank == 0:
@@ -380,6 +380,7 @@ def run_ours(args):
                                    + (", per rank)" if tp else ")"),
                          "achieved": round(achieved_tf, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(achieved_tf / peak_tf, 4), "traffic": traffic,
+                         "traffic_scope": "DRAM bytes of the step's GEMM launches (ncu, profiles/w4a16_gemm_traffic_cfg3.md)",
                          "peak_source": f"{peak_src} bf16_tflops_sustained",
                          "algorithmic_flops_per_step": gemm_flops, "gemm_ms_per_step": round(gemm_ms, 3)},
             "kernels": {
