@@ -19,7 +19,7 @@
 // ldmatrix fragments (K non-transposed, V transposed) with fp32 online
 // softmax in registers.  The loop is HBM-bound (~24 FLOP per KV byte at
 // GQA 4:1 and 6 rows), so the legacy warp MMA is ample; the pool stream is
-// what the kernel is built around: a 4-stage TMA pipeline, 8 KB per stage.
+// what the kernel is built around: an 8-slot TMA ring, 8 KB per page (HD 128).
 // Several splits per sequence (flash-decoding) are merged by
 // attn_combine_kernel in log-sum-exp form.
 #include "common.cuh"
@@ -113,26 +113,35 @@ __device__ __forceinline__ uint32_t q_off(int r, int c) {
   return (uint32_t)(r * (HD * 2) + ((c ^ (r & 7)) << 4));
 }
 
-// One CTA = 16*MT query rows (one row tile of a kv-head group) x one KV
-// split.  Warp 4 is the producer: it keeps a CTA-wide ring of kStages pages
-// full (each page's four 64-column TMA boxes issued by four of its lanes; the
-// split's new-row tiles copied in with plain loads).  Consumer warps 0-3 take
-// the pages round-robin, each with its own online-softmax state over the
-// CTA's rows, and release every slot through an `empty` barrier, so the only
-// CTA-wide barriers are before and after the page loop; the four partial
-// states are merged in shared memory at the end.
+// One CTA = 16*MTW query rows (one row tile of a kv-head group) x one KV
+// split, run by kConsumers page streams of MTW warps each.  Page j of the
+// split goes to stream j % 4; its ring slots are j % kStages (kStages is a
+// multiple of 4, so a stream owns kStages / 4 slots).  The first warp of each
+// stream is also that stream's loader: it fills the stream's slots ahead of
+// use (each page's 64-column TMA boxes issued by a few of its lanes; the
+// split's new-row tiles copied in with plain loads) and refills a slot once
+// all MTW warps of the stream released it through the slot's `empty`
+// barrier.  There is no separate producer warp: two 8-warp CTAs then fit on
+// one SM at 128 registers per thread (four warps per SM sub-partition),
+// enough for the online-softmax state without spilling.  Each warp keeps its
+// own (m, l, O) over its 16 rows; the four streams' partial states are merged
+// in shared memory at the end.
 constexpr int kConsumers = 4;
 
+template <int MTW>
+constexpr int attn_min_ctas() { return MTW == 2 ? 2 : 3; }
+
 template <typename T, int HD, int MTW, int kStages>
-__global__ void __launch_bounds__((kConsumers * MTW + 1) * 32, 2)
+__global__ void __launch_bounds__(kConsumers * MTW * 32, attn_min_ctas<MTW>())
 verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                    const AttnParams p) {
+  static_assert(kStages % kConsumers == 0, "each stream owns whole ring slots");
   constexpr int TILE_BYTES = kPage * HD * 2;  // one tensor, one page
   constexpr int CH = HD / 8;                  // 16-B chunks per row
   constexpr int NBOX = HD / 64;               // 64-column TMA boxes per tile
   constexpr int kRows = 16 * MTW;
   constexpr int MT = 1;  // m16 tiles per consumer warp
-  constexpr int kThreadsAll = (kConsumers * MTW + 1) * 32;
+  constexpr int kThreadsAll = kConsumers * MTW * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *kv_s = smem;                                           // [stage][K, V]
@@ -184,62 +193,59 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
 #pragma unroll
   for (int hr = 0; hr < 2 * MT; ++hr) { m_r[hr] = -INFINITY; l_r[hr] = 0.0f; }
 
-  const int cw = warp % kConsumers;      // page stream of a consumer warp
+  const int cw = warp % kConsumers;            // page stream of this warp
   const int mrow0 = (warp / kConsumers) * 16;  // its m16 tile within the CTA rows
-  if (warp == kConsumers * MTW) {
-    // ---------------- producer ----------------
-    const int pool_rows_per_block = p.L * p.Hkv * kPage;
-    int issued = 0;
-    for (int j = 0; j < ntiles; ++j) {
-      const int t = t_begin + j;
-      const int s = j % kStages;
-      if (j >= kStages && !mbar_wait_warp_sleep(&empty[s], ((uint32_t)(j / kStages) & 1u) ^ 1u, p.timeout_ns)) {
-        abort = true;
-        break;
+  const bool loader = mrow0 == 0;              // first warp of the stream fills its slots
+  const int pool_rows_per_block = p.L * p.Hkv * kPage;
+  // Fill ring slot j % kStages with tile j of this split (loader warp only).
+  auto fill = [&](int j) {
+    const int t = t_begin + j;
+    const int s = j % kStages;
+    uint8_t *st = kv_s + s * 2 * TILE_BYTES;
+    if (tr && lane == 0 && j < 1024) p.trace[j] = clock64();
+    if (t < pc) {
+      int blk = btab[t];
+      if (blk < 0 || blk >= p.total_blocks) {  // invalid page id: record and read page 0 (masked below)
+        if (p.status && lane == 0) atomicExch(p.status, CF_ERANGE);
+        blk = 0;
       }
-      uint8_t *st = kv_s + s * 2 * TILE_BYTES;
-      if (tr && lane == 0 && j < 1024) p.trace[j] = clock64();
-      if (t < pc) {
-        int blk = btab[t];
-        if (blk < 0 || blk >= p.total_blocks) {  // invalid page id: record and read page 0 (masked below)
-          if (p.status && lane == 0) atomicExch(p.status, CF_ERANGE);
-          blk = 0;
+      const int y = blk * pool_rows_per_block + (p.layer * p.Hkv + h) * kPage;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
+      __syncwarp();
+      if (lane < NBOX) tma_load_2d(st + lane * kPage * 128, &tm_k, &full[s], lane * 64, y);
+      else if (lane < 2 * NBOX)
+        tma_load_2d(st + TILE_BYTES + (lane - NBOX) * kPage * 128, &tm_v, &full[s], (lane - NBOX) * 64, y);
+    } else {
+      // new rows (t - pc)*16 ..: this step's K/V scratch rows (plain loads)
+      const int j0 = (t - pc) * kPage;
+      for (int idx = lane; idx < kPage * CH; idx += 32) {
+        const int r = idx / CH, c = idx % CH;
+        const int jr = j0 + r;
+        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+        if (jr < p.R) {
+          const int64_t off = ((int64_t)(b * p.R + jr) * p.Hkv + h) * HD + c * 8;
+          kv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.k_new) + off);
+          vv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.v_new) + off);
         }
-        const int y = blk * pool_rows_per_block + (p.layer * p.Hkv + h) * kPage;
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
-        __syncwarp();
-        if (lane < NBOX) tma_load_2d(st + lane * kPage * 128, &tm_k, &full[s], lane * 64, y);
-        else if (lane < 2 * NBOX)
-          tma_load_2d(st + TILE_BYTES + (lane - NBOX) * kPage * 128, &tm_v, &full[s], (lane - NBOX) * 64, y);
-        issued = j + 1;
-      } else {
-        // new rows (t - pc)*16 ..: this step's K/V scratch rows (plain loads)
-        const int j0 = (t - pc) * kPage;
-        for (int idx = lane; idx < kPage * CH; idx += 32) {
-          const int r = idx / CH, c = idx % CH;
-          const int jr = j0 + r;
-          uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-          if (jr < p.R) {
-            const int64_t off = ((int64_t)(b * p.R + jr) * p.Hkv + h) * HD + c * 8;
-            kv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.k_new) + off);
-            vv = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(p.v_new) + off);
-          }
-          *reinterpret_cast<uint4 *>(st + kv_off<HD>(r, c)) = kv;
-          *reinterpret_cast<uint4 *>(st + TILE_BYTES + kv_off<HD>(r, c)) = vv;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full[s]);  // release: the rows are visible to the consumer
+        *reinterpret_cast<uint4 *>(st + kv_off<HD>(r, c)) = kv;
+        *reinterpret_cast<uint4 *>(st + TILE_BYTES + kv_off<HD>(r, c)) = vv;
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);  // release: the rows are visible to the stream's warps
     }
-    if (abort)  // let our own copies land before the CTA can exit
-      for (int jj = max(0, issued - kStages); jj < issued; ++jj)
-        if (t_begin + jj < pc) mbar_wait_warp(&full[jj % kStages], (uint32_t)(jj / kStages) & 1u, kDrainNs);
-  } else {
+  };
+  int last_issued = cw - kConsumers;  // highest tile this loader has filled
+  if (loader)
+    for (int j = cw; j < min(ntiles, kStages); j += kConsumers) { fill(j); last_issued = j; }
+
+  {
     // ---------------- consumers: page j goes to the MTW warps of stream j % 4 ----------------
     const uint32_t q_base = smem_u32(q_s);
+    int pending_from = cw;  // first filled tile not yet known to have landed (drained on abort)
     for (int j = cw; j < ntiles; j += kConsumers) {
       const int t = t_begin + j;
       const int s = j % kStages;
+      pending_from = j;
       if (!mbar_wait_warp_sleep(&full[s], (uint32_t)(j / kStages) & 1u, p.timeout_ns)) { abort = true; break; }
       if (tr && lane == 0 && mrow0 == 0 && j < 1024) p.trace[1024 + j] = clock64();
       const uint32_t k_base = smem_u32(kv_s + s * 2 * TILE_BYTES), v_base = k_base + TILE_BYTES;
@@ -367,7 +373,17 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);  // slot s may be refilled
       if (tr && lane == 0 && mrow0 == 0 && j < 1024) p.trace[2048 + j] = clock64();
+      if (loader && j + kStages < ntiles) {
+        // every warp of the stream is done with tile j: refill its slot with tile j + kStages
+        pending_from = j + kConsumers;
+        if (!mbar_wait_warp_sleep(&empty[s], (uint32_t)(j / kStages) & 1u, p.timeout_ns)) { abort = true; break; }
+        fill(j + kStages);
+        last_issued = j + kStages;
+      }
     }
+    if (abort && loader)  // let this warp's own copies land before the CTA can exit
+      for (int jj = pending_from; jj <= last_issued; jj += kConsumers)
+        if (t_begin + jj < pc) mbar_wait_warp(&full[jj % kStages], (uint32_t)(jj / kStages) & 1u, kDrainNs);
   }
   if (abort && p.status && lane == 0) atomicExch(p.status, CF_ETIMEOUT);
   const int any_abort = __syncthreads_or(abort ? 1 : 0);
@@ -381,7 +397,6 @@ verify_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
   float *so = reinterpret_cast<float *>(kv_s);            // [stream][rows][HD]
   float *sm_ = so + kConsumers * kRows * HD;                // [stream][rows]
   float *sl = sm_ + kConsumers * kRows;                     // [stream][rows]
-  if (warp < kConsumers * MTW)  // the producer holds no softmax state
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -518,7 +533,7 @@ int launch(const cf_attn_args &a, cudaStream_t stream) {
   CF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   CF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
   dim3 grid(row_tiles, p.B * p.Hkv, p.nsplit);
-  kern<<<grid, (kConsumers * MT + 1) * 32, smem, stream>>>(tk, tv, p);
+  kern<<<grid, kConsumers * MT * 32, smem, stream>>>(tk, tv, p);
   if (cudaGetLastError() != cudaSuccess) return CF_ECUDA;
   if (p.nsplit > 1) {
     dim3 g2(p.B * p.Hkv, p.rows_total);
