@@ -6,8 +6,10 @@ T=1.0, paged KV block 16).
 
 A step = target verify forward over K+1 rows per sequence + fused acceptance
 + page-table commit and K/V commit (cudaforge_b200.BatchVerifier.step).  The
-draft model runs once before timing (its cost is excluded from the metric);
-every step uses fresh uniforms.  Requests are batch-sharded: each rank owns
+draft model (cudaforge_b200.BatchDrafter) drafts once before timing and its
+cost is excluded from the metric; every step uses fresh uniforms.  A second
+timed loop reports full rounds (draft loop + verify step + draft advance) as
+`speculative_round`.  Requests are batch-sharded: each rank owns
 64 sequences with its own weights, pools and page tables and no collective
 (weak scaling).
 
@@ -149,18 +151,18 @@ def setup(args, rank, device):
     ver.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
     gd = torch.Generator(device=device).manual_seed(11 + rank)
     ver.fill_synthetic_kv(gd)
-    # draft: the 1B-shaped INT4 model proposes K tokens per sequence (untimed)
+    # draft: the 1B-shaped INT4 model proposes K tokens per sequence through the device-resident
+    # draft loop (its first round gives the drafts the verify steps reuse; rounds are timed separately)
+    from cudaforge_b200.drafter import BatchDrafter
     draft = LlamaModel(dcfg, device=device, seed=2000 + rank)
-    dcache = draft.make_cache(B * (math.ceil((P + K + 2) / 16) + 2) + 8, max_batch=B)
-    dr = PagedRunner(draft, dcache, list(range(B)))
-    dr.register(prompts[:, :-1].tolist())
+    dcache = draft.make_cache(B * blocks_per_seq + 8, max_batch=B, max_blocks_per_seq=blocks_per_seq + 4)
+    drafter = BatchDrafter(draft, dcache, list(range(B)), K, temperature=args.temperature,
+                           max_blocks_per_seq=blocks_per_seq + 4, use_graph=not args.no_graph)
+    drafter.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
     fill_random(dcache, gd)
-    eng = SpeculativeEngine(dr, None, num_speculative_tokens=K, temperature=args.temperature, seed=3 + rank)
-    eng.target_runner = dr  # device lookup only
-    draft_tokens, draft_logits = eng.draft(prompts.tolist())
-    del dr, dcache, draft
-    torch.cuda.empty_cache()
-    return tcfg, target, cache, ver, draft_tokens.contiguous(), draft_logits.contiguous()
+    du = torch.rand(B, K, generator=gd, device=device)
+    draft_tokens, draft_logits = drafter.draft(du)
+    return tcfg, target, cache, ver, draft_tokens.clone(), draft_logits.clone(), drafter
 
 
 def setup_tp(args, rank, world, device):
@@ -247,10 +249,13 @@ def run_ours(args):
     torch.cuda.set_device(device)
     tree = args.config == "8b-tree"
     tp = args.config == "70b-tp"
+    drafter = None
     if tp:
         tcfg, target, cache, ver, dtok, dlog = setup_tp(args, rank, world, device)
+    elif tree:
+        tcfg, target, cache, ver, dtok, dlog = setup_tree(args, rank, device)
     else:
-        tcfg, target, cache, ver, dtok, dlog = (setup_tree if tree else setup)(args, rank, device)
+        tcfg, target, cache, ver, dtok, dlog, drafter = setup(args, rank, device)
     B = args.batch
     R = dlog.shape[1] if tree else args.k + 1
     K = R - 1
@@ -319,6 +324,34 @@ def run_ours(args):
     h2d = dtok.numel() * 4 + B * R * 4
     d2h = B * R * 4 + B * 4
 
+    # ---- full speculative rounds: draft loop (K steps of the 1B draft) + verify + accept + advance ----
+    round_info = None
+    if drafter is not None:
+        ud = torch.rand(args.steps + 2, B, K, generator=gen, device=device)
+        for i in range(2):  # the drafter captures its graph on its second round
+            dt_, dl_ = drafter.draft(ud[i])
+            r = ver.step(dt_, dl_, uni[i])
+            drafter.advance(r, (ver.n_pinned.clamp_min(0) + 1).tolist())
+        barrier()
+        d_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        r0 = torch.cuda.Event(enable_timing=True)
+        r1 = torch.cuda.Event(enable_timing=True)
+        round_tokens = 0
+        r0.record()
+        for i in range(args.steps):
+            d_ev[i][0].record()
+            dt_, dl_ = drafter.draft(ud[2 + i])
+            d_ev[i][1].record()
+            r = ver.step(dt_, dl_, uni[i])
+            n_host = (ver.n_pinned.clamp_min(0) + 1).tolist()
+            round_tokens += sum(n_host)
+            drafter.advance(r, n_host)
+        r1.record()
+        barrier()
+        round_ms = r0.elapsed_time(r1)
+        draft_ms = sum(a.elapsed_time(b) for a, b in d_ev)
+        round_info = [round_ms, draft_ms, float(round_tokens)]
+
     # max over ranks of the device times, sum of the emitted tokens (batch-sharded, no data-path collective)
     from cudaforge_b200.shard import reduce_step_metrics
     (ms_max, e2e_max), (tok_all, e2e_tok_all) = reduce_step_metrics(
@@ -326,6 +359,13 @@ def run_ours(args):
     if tp:  # every rank verifies the same batch: count its tokens once
         tok_all, e2e_tok_all = tok_all / world, e2e_tok_all / world
     value = tok_all / (ms_max / 1e3)
+    round_out = None
+    if round_info is not None:
+        (rms, dms), (rtok,) = reduce_step_metrics(round_info[:2], round_info[2:], device=device)
+        round_out = {"what": "full speculative round: device-resident draft loop (K steps of the 1B INT4 draft, "
+                             "CUDA graph) + verify + accept + KV commit + draft advance, device-resident inputs",
+                     "accepted_tok_s": round(rtok / (rms / 1e3), 1), "ms_per_round": round(rms / args.steps, 3),
+                     "draft_ms_per_round": round(dms / args.steps, 3)}
     e2e_value = e2e_tok_all / (e2e_max / 1e3)
 
     # roofline of the dominant kernel (W4A16 GEMM, tensor bound) and the others
@@ -375,6 +415,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
+            **({"speculative_round": round_out} if round_out else {}),
             "clocks": clocks,
             "roofline": {"bound": "tensor", "kernel": f"w4a16_gemm (tcgen05, all {4 * tcfg.layers + 1} GEMMs of a step"
                                    + (", per rank)" if tp else ")"),
