@@ -314,25 +314,35 @@ __device__ float exact_chain(F f, int64_t V, float r, int64_t *hit, ScanShared &
       int C0, ue;
       grid_of(c0, C0, ue);
       IncMap loc{0, 0};
+      IncMap em[kPerThread];  // this thread's element maps on the current grid (0 outside [pos, n))
 #pragma unroll
       for (int j = 0; j < kPerThread; ++j) {
         const int li = tid * kPerThread + j;
-        if (li >= pos && li < n) loc = compose(loc, elem_map(v[j], ue));
+        em[j] = (li >= pos && li < n) ? elem_map(v[j], ue) : IncMap{0, 0};
+        loc = compose(loc, em[j]);
       }
       const IncMap pre = block_exclusive_scan(loc, sh);  // its barriers order the resets above
       int C = apply(pre, C0);
       if (C >= kTop) C = kTop;  // a crossing lies before this thread's elements
       int my_cross = INT_MAX, my_found = INT_MAX;
-      if (C < kTop) {
+      // The running value only grows, so the exact value after this thread's last element
+      // (apply(loc, C), below kTop exactly when no element of the range leaves the grid) tells
+      // whether the range holds a crossing or, when searching, the first r <= cum: most
+      // threads then skip the element walk.
+      const int Cend = C < kTop ? apply(loc, C) : kTop;
+      const bool walk = C < kTop && (Cend >= kTop || (SEARCH && r <= ldexpf((float)Cend, ue)));
+      if (walk) {
 #pragma unroll
         for (int j = 0; j < kPerThread; ++j) {
           const int li = tid * kPerThread + j;
           if (li < pos || li >= n || my_cross != INT_MAX || my_found != INT_MAX) continue;
-          const int Cn = apply(elem_map(v[j], ue), C);
+          const int Cn = apply(em[j], C);
           if (Cn >= kTop) { my_cross = li; continue; }
           C = Cn;
           if (SEARCH && r <= ldexpf((float)C, ue)) my_found = li;
         }
+      } else if (C < kTop) {
+        C = Cend;
       }
       if (my_cross != INT_MAX) atomicMin(&sh.cross, my_cross);
       if (my_found != INT_MAX) atomicMin(&sh.found, my_found);
@@ -354,7 +364,7 @@ __device__ float exact_chain(F f, int64_t V, float r, int64_t *hit, ScanShared &
 #pragma unroll
         for (int j = 0; j < kPerThread; ++j) {
           const int li = tid * kPerThread + j;
-          if (li >= pos && li < cross) Cp = apply(elem_map(v[j], ue), Cp);
+          if (li >= pos && li < cross) Cp = apply(em[j], Cp);
         }
         const float cprev = ldexpf((float)Cp, ue);  // exact: Cp < 2^24 on the 2^ue grid
         float vx = 0.0f;
@@ -414,7 +424,7 @@ __device__ int64_t block_argmax(const T *x, int64_t V, float c, RowStat st) {
 enum Mode : int { kDone = 0, kResidual = 1, kBonus = 2 };
 
 template <typename T>
-__global__ void __launch_bounds__(kDecideThreads)
+__global__ void __launch_bounds__(kDecideThreads, 1)
 decide_kernel(cf_accept_args a, float c, const RowStat *stats) {
   __shared__ ScanShared sh;
   __shared__ int s_mode, s_row, s_na;
@@ -554,7 +564,7 @@ struct TreeArgs {
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kDecideThreads)
+__global__ void __launch_bounds__(kDecideThreads, 1)
 decide_tree_kernel(TreeArgs ta, float c, const RowStat *stats) {
   __shared__ ScanShared sh;
   __shared__ int s_cur, s_moved, s_any, s_used, s_resid, s_done, s_na;
