@@ -468,20 +468,23 @@ __global__ void attn_combine_kernel(const AttnParams p) {
   }
 }
 
-int attn_mt() {
+// Row tiles of 16 query rows per page stream: 1 when a kv-head group's rows fit
+// in 16 (decode-like steps: fewer idle MMA rows, up to three CTAs per SM), else 2.
+int attn_mt(int rows_total) {
   const char *v = getenv("CF_ATTN_MT");
-  return v ? atoi(v) : 2;
+  if (v && atoi(v) > 0) return atoi(v) == 1 ? 1 : 2;
+  return rows_total <= 16 ? 1 : 2;
 }
 
-int pick_splits(const cf_attn_args &a, int row_tiles) {
+int pick_splits(const cf_attn_args &a, int row_tiles, int per_sm) {
   if (a.num_splits > 0) return a.num_splits;
   int sms = 148;
   int dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int ctas = a.batch * a.kv.num_kv_heads * row_tiles;
-  // two resident CTAs per SM: split the context only when the grid would not fill them
-  const int want = ctas >= 2 * sms ? 1 : (2 * sms + ctas - 1) / ctas;
+  // per_sm resident CTAs per SM: split the context only when the grid would not fill them
+  const int want = ctas >= per_sm * sms ? 1 : (per_sm * sms + ctas - 1) / ctas;
   const int pages = (a.max_context + kPage - 1) / kPage;
   return std::max(1, std::min(want, std::max(1, pages / 8)));
 }
@@ -494,7 +497,7 @@ int launch(const cf_attn_args &a, cudaStream_t stream) {
   p.B = a.batch; p.R = a.rows; p.G = G; p.Hkv = a.kv.num_kv_heads; p.L = a.kv.num_layers; p.layer = a.layer;
   p.rows_total = a.rows * G;
   const int row_tiles = (p.rows_total + ROWS - 1) / ROWS;
-  p.nsplit = pick_splits(a, row_tiles);
+  p.nsplit = pick_splits(a, row_tiles, attn_min_ctas<MT>());
   p.max_blocks = a.max_blocks; p.total_blocks = a.kv.total_blocks;
   p.q = a.q; p.q_row_stride = a.q_row_stride;
   const int64_t layer_new = (int64_t)a.batch * a.rows * p.Hkv * HD;
@@ -544,7 +547,7 @@ int launch(const cf_attn_args &a, cudaStream_t stream) {
 
 template <typename T>
 int dispatch(const cf_attn_args &a, cudaStream_t s) {
-  const int mt = attn_mt();
+  const int mt = attn_mt(a.rows * (a.num_q_heads / a.kv.num_kv_heads));
   if (a.kv.head_dim == 128) return mt == 2 ? launch<T, 128, 2, 8>(a, s) : launch<T, 128, 1, 8>(a, s);
   if (a.kv.head_dim == 64) return mt == 2 ? launch<T, 64, 2, 8>(a, s) : launch<T, 64, 1, 8>(a, s);
   return CF_EUNSUPPORTED;
@@ -556,8 +559,9 @@ extern "C" size_t cf_attention_workspace_bytes(const cf_attn_args *a) {
   if (!a || a->kv.num_kv_heads <= 0 || a->num_q_heads % a->kv.num_kv_heads) return 0;
   const int G = a->num_q_heads / a->kv.num_kv_heads;
   const int rows_total = a->rows * G;
-  const int ROWS = 16 * attn_mt();
-  const int nsplit = pick_splits(*a, (rows_total + ROWS - 1) / ROWS);
+  const int mt = attn_mt(rows_total);
+  const int ROWS = 16 * mt;
+  const int nsplit = pick_splits(*a, (rows_total + ROWS - 1) / ROWS, mt == 2 ? attn_min_ctas<2>() : attn_min_ctas<1>());
   if (nsplit <= 1) return 0;
   const size_t rows = (size_t)nsplit * a->batch * a->kv.num_kv_heads * rows_total;
   return rows * a->kv.head_dim * sizeof(float) + rows * sizeof(float);
