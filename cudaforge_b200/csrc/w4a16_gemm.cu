@@ -100,11 +100,8 @@ template <typename T> __device__ __forceinline__ T from_f(float v);
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
-// MINB = CTAs per SM the launch is built for: 1 (512 TMEM columns, deep rings) or,
-// for token slices of <= 64 rows, 2 (256 TMEM columns, shallow rings) so that two
-// CTAs' pipelines overlap their hand-off latencies on one SM.
-template <typename T, int WM, int MINB>
-__global__ void __launch_bounds__(kThreads, MINB)
+template <typename T, int WM>
+__global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
             const __grid_constant__ CUtensorMap tm_s, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -392,7 +389,7 @@ __global__ void repack_kernel(const uint32_t *src, uint32_t *dst, int64_t n_word
 }
 
 struct Plan {
-  int slices, m_slice, splits, kb_per_split, sa, sx, sw, ntiles, per_sm;
+  int slices, m_slice, splits, kb_per_split, sa, sx, sw, ntiles;
   uint32_t x_bytes, off_x, off_w, off_bar, tmem_cols, a_tcol;
   size_t smem;
 };
@@ -420,19 +417,17 @@ bool make_plan(int M, int N, int K, int split_req, bool int4, Plan &pl) {
   const size_t budget = kMaxSmem - 1024 - 1024;  // alignment slack + barriers
   const size_t w_stage = int4 ? kWStageBytes : 0;
   auto env = [](const char *n, int d) { const char *v = getenv(n); return v ? atoi(v) : d; };
-  // small token slices: two CTAs per SM (half the TMEM, shallow rings, <= ~110 KB smem each)
-  pl.per_sm = (int4 && pl.m_slice <= 64 && env("CF_GEMM_TWO", 1)) ? 2 : 1;
   if (int4) {
     pl.a_tcol = (2u * pl.m_slice + 31u) & ~31u;
-    pl.tmem_cols = pl.per_sm == 2 ? 256u : 512u;
-    pl.sa = std::min(env("CF_GEMM_SA", 4), (int)((pl.tmem_cols - pl.a_tcol) / 64u));
+    pl.sa = std::min(env("CF_GEMM_SA", 4), (int)((512u - pl.a_tcol) / 64u));
+    pl.tmem_cols = 512;
   } else {
     pl.a_tcol = 0;
     pl.sa = env("CF_GEMM_SA", 3);
   }
   const size_t a_bytes = int4 ? (size_t)kAStageBytes : pl.sa * (size_t)kAStageBytes;
-  pl.sw = int4 ? env("CF_GEMM_SW", pl.per_sm == 2 ? 4 : 8) : 1;
-  pl.sx = (int)std::min<size_t>(env("CF_GEMM_SX", pl.per_sm == 2 ? 4 : 6), (budget - a_bytes - pl.sw * w_stage) / pl.x_bytes);
+  pl.sw = int4 ? env("CF_GEMM_SW", 8) : 1;
+  pl.sx = (int)std::min<size_t>(env("CF_GEMM_SX", 6), (budget - a_bytes - pl.sw * w_stage) / pl.x_bytes);
   if (pl.sx < 2 && !int4) { pl.sa = 2; pl.sx = (int)std::min<size_t>(4, (budget - 2 * (size_t)kAStageBytes) / pl.x_bytes); }
   if (pl.sx < 2 || pl.sa < 2 || (int4 && pl.sw < 2)) return false;
   pl.off_x = (uint32_t)(int4 ? kAStageBytes : pl.sa * kAStageBytes);
@@ -508,7 +503,7 @@ int run_gemm(const cf_gemm_args &a, cudaStream_t stream) {
   p.status = a.status;
   p.timeout_ns = a.timeout_ns ? a.timeout_ns : 2000000000ull;
   p.trace = reinterpret_cast<unsigned long long *>(a.trace);
-  auto kern = pl.per_sm == 2 ? gemm_kernel<T, WM, 2> : gemm_kernel<T, WM, 1>;
+  auto kern = gemm_kernel<T, WM>;
   CF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
   dim3 grid(pl.slices, pl.ntiles, pl.splits);
   kern<<<grid, kThreads, pl.smem, stream>>>(tx, tw, ts, p);
