@@ -274,6 +274,7 @@ def run_ours(args):
     # ---- timed region (device-resident inputs) ----
     clk = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
     clk.start()
+    time.sleep(0.5)  # nvidia-smi's first sample takes a moment; the samples span every timed loop below
     tokens_per_step = []
     l0 = _lib.LAUNCHES[0]
     barrier()
@@ -285,7 +286,6 @@ def run_ours(args):
         tokens_per_step.append(int((ver.n_pinned.clamp_min(0) + 1).sum()))
     e1.record()
     barrier()
-    clocks = clk.stop()
     launches = _lib.LAUNCHES[0] - l0
     ms = e0.elapsed_time(e1)
     # ---- per-kernel timing pass (same step, CUDA events around every launch group) ----
@@ -352,6 +352,8 @@ def run_ours(args):
         draft_ms = sum(a.elapsed_time(b) for a, b in d_ev)
         round_info = [round_ms, draft_ms, float(round_tokens)]
 
+    clocks = clk.stop()
+    clocks["window"] = "headline, per-kernel, e2e and full-round timed loops"
     # max over ranks of the device times, sum of the emitted tokens (batch-sharded, no data-path collective)
     from cudaforge_b200.shard import reduce_step_metrics
     (ms_max, e2e_max), (tok_all, e2e_tok_all) = reduce_step_metrics(
