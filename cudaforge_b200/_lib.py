@@ -126,6 +126,12 @@ def lib() -> ctypes.CDLL:
         L.cf_rmsnorm.argtypes = [_P, _I64, _P, _P, _I64, _I32, _I32, _F32, _I32, _P]
         L.cf_rope_qkv.argtypes = [_P, _I64, _I32, _I32, _I32, _I32, _P, _F32, _P, _P, _I32, _P]
         L.cf_silu_mul.argtypes = [_P, _I64, _P, _I64, _I32, _I32, _I32, _P]
+        L.cf_gemm_splits.argtypes = [_I32, _I32, _I32, _I32, _I32]
+        for fn in ("cf_w4a16_gemm_partials", "cf_dense_gemm_partials"):
+            getattr(L, fn).argtypes = [ctypes.POINTER(CfGemmArgs), _P]
+        L.cf_splitk_rmsnorm.argtypes = [_P, _I32, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _I64, _F32, _I32, _P]
+        L.cf_splitk_rope_qkv.argtypes = [_P, _I32, _I32, _P, _I64, _I32, _I32, _I32, _P, _F32, _P, _P, _I32, _P]
+        L.cf_splitk_silu_mul.argtypes = [_P, _I32, _I32, _I32, _P, _I64, _I32, _P]
         _lib = L
     return _lib
 

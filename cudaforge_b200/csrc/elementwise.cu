@@ -108,6 +108,142 @@ __global__ void silu_mul_kernel(const T *gu, int64_t ldg, T *out, int64_t ldo, i
   }
 }
 
+// ---------------------------------------------------------------------------
+// Split-K consumers: the producing GEMM left `splits` fp32 partials
+// [splits][m][n] (cf_w4a16_gemm_partials); each kernel below first forms the
+// GEMM output exactly as the split-K reduction would (fixed order s = 0..S-1,
+// then + residual, then one rounding to T) and then does its own work on those
+// values, so the result is bit-identical to reduce-then-consume.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void reduce8(const float *part, int splits, int64_t plane, int64_t off, const T *res,
+                                        float (&o)[8]) {
+  float4 a = *reinterpret_cast<const float4 *>(part + off), b = *reinterpret_cast<const float4 *>(part + off + 4);
+  for (int s = 1; s < splits; ++s) {
+    const float4 c = *reinterpret_cast<const float4 *>(part + s * plane + off);
+    const float4 d = *reinterpret_cast<const float4 *>(part + s * plane + off + 4);
+    a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
+    b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
+  }
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+  if (res) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] += cf::to_float(res[j]);
+  }
+}
+
+// y = T(sum of partials + residual) (written, the residual stream); out = RMSNorm(y) * w.
+template <typename T>
+__global__ void splitk_rmsnorm_kernel(const float *part, int splits, int64_t plane, int n, const T *res,
+                                      int64_t ldr, T *y, int64_t ldy, const T *w, T *out, int64_t ldo, int dim,
+                                      float eps) {
+  const int m = blockIdx.x;
+  T *yr = y + (int64_t)m * ldy;
+  float ss = 0.0f;
+  for (int v = threadIdx.x; v < dim / 8; v += blockDim.x) {
+    float f8[8];
+    reduce8<T>(part, splits, plane, (int64_t)m * n + v * 8, res ? res + (int64_t)m * ldr + v * 8 : nullptr, f8);
+    uint4 o;
+    T *op = reinterpret_cast<T *>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) op[j] = from_f<T>(f8[j]);
+    reinterpret_cast<uint4 *>(yr)[v] = o;
+    cf::Vec16<T> pk;
+    pk.raw = o;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { const float f = pk.get(j); ss += f * f; }
+  }
+  ss = cf::warp_sum(ss);
+  __shared__ float red[32];
+  const int w_ = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w_] = ss;
+  __syncthreads();
+  if (w_ == 0) {
+    ss = l < (int)(blockDim.x >> 5) ? red[l] : 0.0f;
+    ss = cf::warp_sum(ss);
+    if (l == 0) red[0] = ss;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)dim + eps);
+  T *orow = out + (int64_t)m * ldo;
+  for (int v = threadIdx.x; v < dim / 8; v += blockDim.x) {
+    cf::Vec16<T> pk, pw;
+    pk.raw = reinterpret_cast<const uint4 *>(yr)[v];  // this thread's own values, written above
+    pw.raw = reinterpret_cast<const uint4 *>(w)[v];
+    uint4 o;
+    T *op = reinterpret_cast<T *>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) op[j] = from_f<T>(pk.get(j) * inv * pw.get(j));
+    reinterpret_cast<uint4 *>(orow)[v] = o;
+  }
+}
+
+// The RoPE / K-V scatter of rope_qkv_kernel on T(sum of partials); rotated q goes to qkv.
+template <typename T>
+__global__ void splitk_rope_qkv_kernel(const float *part, int splits, int64_t plane, int n, T *qkv, int64_t ld,
+                                       int Hq, int Hkv, int D, const int32_t *pos, float log2_base, T *k_new,
+                                       T *v_new) {
+  const int m = blockIdx.x;
+  T *row = qkv + (int64_t)m * ld;
+  const float *prow = part + (int64_t)m * n;
+  const float p = (float)pos[m];
+  const int half = D / 2;
+  const int pairs = (Hq + Hkv) * half;
+  auto val = [&](int col) {
+    float a = prow[col];
+    for (int s = 1; s < splits; ++s) a += prow[s * plane + col];
+    return cf::to_float(from_f<T>(a));
+  };
+  for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
+    const int hh = idx / half, i = idx % half;
+    const float inv_freq = exp2f(-((float)(2 * i) / (float)D) * log2_base);
+    float s, c;
+    sincosf(p * inv_freq, &s, &c);
+    const float x1 = val(hh * D + i), x2 = val(hh * D + i + half);
+    const float o1 = x1 * c - x2 * s, o2 = x1 * s + x2 * c;
+    if (hh < Hq) {
+      row[(int64_t)hh * D + i] = from_f<T>(o1);
+      row[(int64_t)hh * D + i + half] = from_f<T>(o2);
+    } else {
+      T *dst = k_new + ((int64_t)m * Hkv + (hh - Hq)) * D;
+      dst[i] = from_f<T>(o1);
+      dst[i + half] = from_f<T>(o2);
+    }
+  }
+  T *vdst = v_new + (int64_t)m * Hkv * D;
+  const int v0 = (Hq + Hkv) * D;
+  for (int v = threadIdx.x; v < Hkv * D / 8; v += blockDim.x) {
+    float f8[8];
+    reduce8<T>(part, splits, plane, (int64_t)m * n + v0 + v * 8, nullptr, f8);
+    uint4 o;
+    T *op = reinterpret_cast<T *>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) op[j] = from_f<T>(f8[j]);
+    reinterpret_cast<uint4 *>(vdst)[v] = o;
+  }
+}
+
+// SwiGLU on T(sum of partials) of the fused gate|up rows.
+template <typename T>
+__global__ void splitk_silu_mul_kernel(const float *part, int splits, int64_t plane, int n, T *out, int64_t ldo,
+                                       int ffn) {
+  const int m = blockIdx.y;
+  T *o = out + (int64_t)m * ldo;
+  for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < ffn / 8; v += gridDim.x * blockDim.x) {
+    float g8[8], u8[8];
+    reduce8<T>(part, splits, plane, (int64_t)m * n + v * 8, nullptr, g8);
+    reduce8<T>(part, splits, plane, (int64_t)m * n + ffn + v * 8, nullptr, u8);
+    uint4 r;
+    T *rp = reinterpret_cast<T *>(&r);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float x = cf::to_float(from_f<T>(g8[j]));
+      rp[j] = from_f<T>(x / (1.0f + expf(-x)) * cf::to_float(from_f<T>(u8[j])));
+    }
+    reinterpret_cast<uint4 *>(o)[v] = r;
+  }
+}
+
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -174,6 +310,71 @@ extern "C" int cf_silu_mul(const void *gu, int64_t ldg, void *out, int64_t ldo, 
     silu_mul_kernel<<<grid, 256, 0, s>>>((const __nv_bfloat16 *)gu, ldg, (__nv_bfloat16 *)out, ldo, ffn);
   else if (dtype == CF_F16)
     silu_mul_kernel<<<grid, 256, 0, s>>>((const __half *)gu, ldg, (__half *)out, ldo, ffn);
+  else
+    return CF_EINVAL;
+  return cf_launch_status();
+}
+
+extern "C" int cf_splitk_rmsnorm(const float *partials, int32_t splits, int32_t m, int32_t n, const void *residual,
+                                 int64_t ldr, void *y, int64_t ldy, const void *w, void *out, int64_t ldo, float eps,
+                                 int32_t dtype, void *stream) {
+  if (m < 0 || n <= 0 || n % 8 || splits < 1 || ldy % 8 || ldo % 8 || (residual && ldr % 8)) return CF_EINVAL;
+  if (!partials || !y || !w || !out || !aligned16(partials) || !aligned16(y) || !aligned16(w) || !aligned16(out))
+    return CF_EINVAL;
+  if (m == 0) return CF_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int threads = n >= 4096 ? 512 : 128;  // as cf_rmsnorm: the same reduction order
+  const int64_t plane = (int64_t)m * n;
+  if (dtype == CF_BF16)
+    splitk_rmsnorm_kernel<<<m, threads, 0, s>>>(partials, splits, plane, n, (const __nv_bfloat16 *)residual, ldr,
+                                                (__nv_bfloat16 *)y, ldy, (const __nv_bfloat16 *)w,
+                                                (__nv_bfloat16 *)out, ldo, n, eps);
+  else if (dtype == CF_F16)
+    splitk_rmsnorm_kernel<<<m, threads, 0, s>>>(partials, splits, plane, n, (const __half *)residual, ldr,
+                                                (__half *)y, ldy, (const __half *)w, (__half *)out, ldo, n, eps);
+  else
+    return CF_EINVAL;
+  return cf_launch_status();
+}
+
+extern "C" int cf_splitk_rope_qkv(const float *partials, int32_t splits, int32_t m, void *qkv, int64_t ld,
+                                  int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const int32_t *pos,
+                                  float base, void *k_new, void *v_new, int32_t dtype, void *stream) {
+  if (m < 0 || splits < 1 || head_dim % 16 || num_q_heads <= 0 || num_kv_heads <= 0 || !partials || !qkv || !pos ||
+      !k_new || !v_new)
+    return CF_EINVAL;
+  if (ld % 8 || !aligned16(partials) || !aligned16(qkv) || !aligned16(v_new) || !(base > 1.0f)) return CF_EINVAL;
+  if (m == 0) return CF_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const float lb = log2f(base);
+  const int n = (num_q_heads + 2 * num_kv_heads) * head_dim;
+  const int64_t plane = (int64_t)m * n;
+  if (dtype == CF_BF16)
+    splitk_rope_qkv_kernel<<<m, 256, 0, s>>>(partials, splits, plane, n, (__nv_bfloat16 *)qkv, ld, num_q_heads,
+                                             num_kv_heads, head_dim, pos, lb, (__nv_bfloat16 *)k_new,
+                                             (__nv_bfloat16 *)v_new);
+  else if (dtype == CF_F16)
+    splitk_rope_qkv_kernel<<<m, 256, 0, s>>>(partials, splits, plane, n, (__half *)qkv, ld, num_q_heads,
+                                             num_kv_heads, head_dim, pos, lb, (__half *)k_new, (__half *)v_new);
+  else
+    return CF_EINVAL;
+  return cf_launch_status();
+}
+
+extern "C" int cf_splitk_silu_mul(const float *partials, int32_t splits, int32_t m, int32_t ffn, void *out,
+                                  int64_t ldo, int32_t dtype, void *stream) {
+  if (m < 0 || splits < 1 || ffn <= 0 || ffn % 8 || ldo % 8 || !partials || !out || !aligned16(partials) ||
+      !aligned16(out))
+    return CF_EINVAL;
+  if (m == 0) return CF_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid((ffn / 8 + 255) / 256, m);
+  const int n = 2 * ffn;
+  const int64_t plane = (int64_t)m * n;
+  if (dtype == CF_BF16)
+    splitk_silu_mul_kernel<<<grid, 256, 0, s>>>(partials, splits, plane, n, (__nv_bfloat16 *)out, ldo, ffn);
+  else if (dtype == CF_F16)
+    splitk_silu_mul_kernel<<<grid, 256, 0, s>>>(partials, splits, plane, n, (__half *)out, ldo, ffn);
   else
     return CF_EINVAL;
   return cf_launch_status();

@@ -449,8 +449,10 @@ bool make_plan(int M, int N, int K, int split_req, bool int4, Plan &pl) {
   return true;
 }
 
+// partials_only: when the plan splits K, leave the fp32 partials [splits][m][n] in the
+// workspace for a fused consumer (cf_splitk_*) instead of launching the reduction.
 template <typename T, int WM>
-int run_gemm(const cf_gemm_args &a, cudaStream_t stream) {
+int run_gemm(const cf_gemm_args &a, cudaStream_t stream, bool partials_only = false) {
   const bool int4 = WM == kInt4;
   if (a.m < 0 || a.n <= 0 || a.k <= 0) return CF_EINVAL;
   if (a.m == 0) return CF_OK;
@@ -508,7 +510,7 @@ int run_gemm(const cf_gemm_args &a, cudaStream_t stream) {
   dim3 grid(pl.slices, pl.ntiles, pl.splits);
   kern<<<grid, kThreads, pl.smem, stream>>>(tx, tw, ts, p);
   if (cudaGetLastError() != cudaSuccess) return CF_ECUDA;
-  if (pl.splits > 1) {
+  if (pl.splits > 1 && !partials_only) {
     const int64_t total4 = (int64_t)a.m * a.n / 4;
     const int blocks = (int)std::min<int64_t>((total4 + 255) / 256, (int64_t)num_sms() * 8);
     splitk_reduce_kernel<T><<<blocks, 256, 0, stream>>>(p.partial, pl.splits, a.m, a.n, reinterpret_cast<T *>(a.y),
@@ -536,6 +538,26 @@ extern "C" int cf_dense_gemm(const cf_gemm_args *args, void *stream) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (args->act_dtype == CF_BF16) return run_gemm<__nv_bfloat16, kDense>(*args, s);
   if (args->act_dtype == CF_F16) return run_gemm<__half, kDense>(*args, s);
+  return CF_EUNSUPPORTED;
+}
+
+extern "C" int cf_gemm_splits(int32_t m, int32_t n, int32_t k, int32_t split_k, int32_t int4) {
+  Plan pl;
+  if (m <= 0 || n <= 0 || k <= 0 || !make_plan(m, n, k, split_k, int4 != 0, pl)) return 0;
+  return pl.splits;
+}
+
+extern "C" int cf_w4a16_gemm_partials(const cf_gemm_args *args, void *stream) {
+  if (!args) return CF_EINVAL;
+  if (args->act_dtype != CF_BF16) return CF_EUNSUPPORTED;
+  return run_gemm<__nv_bfloat16, kInt4>(*args, reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+extern "C" int cf_dense_gemm_partials(const cf_gemm_args *args, void *stream) {
+  if (!args) return CF_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (args->act_dtype == CF_BF16) return run_gemm<__nv_bfloat16, kDense>(*args, s, true);
+  if (args->act_dtype == CF_F16) return run_gemm<__half, kDense>(*args, s, true);
   return CF_EUNSUPPORTED;
 }
 

@@ -49,6 +49,9 @@ def repack_int4(wq: torch.Tensor, stream=None) -> torch.Tensor:
     return out
 
 
+MAX_FUSED_SPLITS = 4
+
+
 class _Ws:
     """Per-device cached split-K workspace (grown on demand)."""
     bufs: dict = {}
@@ -63,13 +66,19 @@ class _Ws:
 
 
 def _gemm(fn, x, w, scales, n, residual, out, split_k, workspace, status, int4, timeout_ns=0, stream=None,
-          trace=None):
+          trace=None, partials_fn=None):
     if x.dim() != 2 or x.stride(1) != 1:
         raise ValueError("x must be 2-D with unit inner stride")
     M, K = x.shape
     if out is None:
         out = torch.empty((M, n), dtype=x.dtype, device=x.device)
     L = _lib.lib()
+    splits = L.cf_gemm_splits(M, n, K, split_k, int(int4))
+    # fused consumers add the partials serially per element over fewer threads than the
+    # reduction kernel: worth it for a few splits (the verify shapes), not for many
+    fused = partials_fn is not None and 1 < splits <= MAX_FUSED_SPLITS
+    if fused:
+        fn = partials_fn
     need = L.cf_gemm_workspace_bytes(M, n, K, split_k, int(int4))
     if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
         workspace = _Ws.get(x.device, need)
@@ -83,23 +92,33 @@ def _gemm(fn, x, w, scales, n, residual, out, split_k, workspace, status, int4, 
                         timeout_ns=timeout_ns, trace=trace.data_ptr() if trace is not None else None)
     s = stream or torch.cuda.current_stream(x.device)
     _lib.check(fn(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), fn.__name__)
+    if fused:
+        _lib.count(1)
+        part = workspace.view(-1)[: splits * M * n * 4].view(torch.float32).view(splits, M, n)
+        return part, splits
     _lib.count(2 if need else 1)
     return out
 
 
 def w4a16_gemm(x: torch.Tensor, wq_kernel: torch.Tensor, scales: torch.Tensor, *, residual=None, out=None,
                split_k: int = 0, workspace=None, status=None, timeout_ns: int = 0, stream=None,
-               trace=None) -> torch.Tensor:
-    """y = x @ deq(W) (+ residual); x bf16 [M, K], wq_kernel from repack_int4, scales fp16 [K/128, N]."""
+               trace=None, partials: bool = False):
+    """y = x @ deq(W) (+ residual); x bf16 [M, K], wq_kernel from repack_int4, scales fp16 [K/128, N].
+    partials=True: when the plan splits K into 2..MAX_FUSED_SPLITS pieces, run only the GEMM
+    and return (fp32 partials [splits, M, N] in the workspace, splits) for an ops.splitk_*
+    consumer (residual and out untouched); otherwise y as usual."""
     n = wq_kernel.shape[1]
-    return _gemm(_lib.lib().cf_w4a16_gemm, x, wq_kernel, scales, n, residual, out, split_k, workspace, status,
-                 True, timeout_ns, stream, trace)
+    L = _lib.lib()
+    return _gemm(L.cf_w4a16_gemm, x, wq_kernel, scales, n, residual, out, split_k, workspace, status,
+                 True, timeout_ns, stream, trace, partials_fn=L.cf_w4a16_gemm_partials if partials else None)
 
 
 def dense_gemm(x: torch.Tensor, w: torch.Tensor, *, residual=None, out=None, split_k: int = 0, workspace=None,
-               status=None, stream=None) -> torch.Tensor:
-    """y = x @ w.T (+ residual); x [M, K], w [N, K] (nn.Linear layout), both bf16 or both fp16."""
+               status=None, stream=None, partials: bool = False):
+    """y = x @ w.T (+ residual); x [M, K], w [N, K] (nn.Linear layout), both bf16 or both fp16.
+    partials: as w4a16_gemm."""
     if w.dtype != x.dtype or not w.is_contiguous():
         raise ValueError("w must be contiguous and share x's dtype")
-    return _gemm(_lib.lib().cf_dense_gemm, x, w, None, w.shape[0], residual, out, split_k, workspace, status,
-                 False, 0, stream)
+    L = _lib.lib()
+    return _gemm(L.cf_dense_gemm, x, w, None, w.shape[0], residual, out, split_k, workspace, status,
+                 False, 0, stream, partials_fn=L.cf_dense_gemm_partials if partials else None)

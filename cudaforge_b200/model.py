@@ -110,10 +110,13 @@ class Linear:
             return Linear._wrap("int4", self.n, k1 - k0, wq=self.wq[k0 // 8: k1 // 8], scales=self.scales[k0 // 128: k1 // 128])
         return Linear._wrap(self.quant, self.n, k1 - k0, w=self.w[:, k0:k1])
 
-    def __call__(self, x, out=None, residual=None, workspace=None):
+    def __call__(self, x, out=None, residual=None, workspace=None, partials=False):
+        """y = x W^T (+ residual) into `out`; with partials=True a K-split plan returns
+        (fp32 partials, splits) for an ops.splitk_* consumer instead (out untouched)."""
         if self.quant == "int4":
-            return w4a16_gemm(x, self.wq, self.scales, out=out, residual=residual, workspace=workspace)
-        return dense_gemm(x, self.w, out=out, residual=residual, workspace=workspace)
+            return w4a16_gemm(x, self.wq, self.scales, out=out, residual=residual, workspace=workspace,
+                              partials=partials)
+        return dense_gemm(x, self.w, out=out, residual=residual, workspace=workspace, partials=partials)
 
 
 @dataclasses.dataclass(frozen=True)
@@ -210,6 +213,7 @@ class LlamaModel:
         self.final_norm = (torch.randn(cfg.d_model, generator=g, device=self.device) * 0.02 + 1.0).to(dt)
         self.lm_head = self._shard("lm_head", Linear(cfg.vocab, cfg.d_model, cfg, g, self.device))
         self._bufs = {}
+        self.fuse_splitk = True  # split-K reductions fused into the consuming op (bit-identical)
 
     def _shard(self, name: str, lin: Linear) -> Linear:
         if self.tp is None:
@@ -262,38 +266,61 @@ class LlamaModel:
         bf = self.buffers(B, R)
         h, xn, qkv, attn, gu, act = bf["h"], bf["xn"], bf["qkv"], bf["attn"], bf["gu"], bf["act"]
         T = timer or _null_timer
+        # Split-K GEMMs hand their fp32 partials to the next op, which forms the GEMM output
+        # exactly as the reduction would and fuses its own work (RoPE, residual + RMSNorm,
+        # SwiGLU): no reduction launch.  Not under TP, where an all-reduce sits in between.
+        fuse = tp is None and self.fuse_splitk
+        split = lambda r: isinstance(r, tuple)  # noqa: E731
         with T("other"):
             ops.embedding(tokens.reshape(-1), self.embed, out=h)
+        pending = None  # partials of the previous down projection (+ residual h) not yet reduced
         for li, lay in enumerate(self.layers):
             with T("other"):
-                ops.rmsnorm(h, lay["attn_norm"], c.eps, out=xn)
+                if pending is not None:
+                    ops.splitk_rmsnorm(pending, lay["attn_norm"], y=h, out=xn, residual=h, eps=c.eps)
+                else:
+                    ops.rmsnorm(h, lay["attn_norm"], c.eps, out=xn)
             with T("gemm"):
-                lay["qkv"](xn, out=qkv)
+                r = lay["qkv"](xn, out=qkv, partials=fuse)
             with T("other"):
-                ops.rope_qkv(qkv, positions, c.n_heads, c.n_kv_heads, c.head_dim, bf["k_new"][li], bf["v_new"][li],
-                             base=c.rope_base)
+                if split(r):
+                    ops.splitk_rope_qkv(r, qkv, positions, c.n_heads, c.n_kv_heads, c.head_dim, bf["k_new"][li],
+                                        bf["v_new"][li], base=c.rope_base)
+                else:
+                    ops.rope_qkv(qkv, positions, c.n_heads, c.n_kv_heads, c.head_dim, bf["k_new"][li],
+                                 bf["v_new"][li], base=c.rope_base)
             with T("attn"):
                 ops.verify_attention(cache, li, qkv, bf["k_new"][li], bf["v_new"][li], block_tables, context_lens,
                                      max_context, rows=R, num_q_heads=c.n_heads, out=attn, tree_mask=tree_mask,
                                      status=status)
             with T("gemm"):  # TP: rank 0 carries the residual, the all-reduce sums the partial outputs
-                lay["o"](attn, out=h, residual=h if tp is None or tp.rank == 0 else None)
+                r = lay["o"](attn, out=h, residual=h if tp is None or tp.rank == 0 else None, partials=fuse)
             if tp is not None:
                 with T("comm"):
                     self._all_reduce(h)
             with T("other"):
-                ops.rmsnorm(h, lay["ffn_norm"], c.eps, out=xn)
+                if split(r):
+                    ops.splitk_rmsnorm(r, lay["ffn_norm"], y=h, out=xn, residual=h, eps=c.eps)
+                else:
+                    ops.rmsnorm(h, lay["ffn_norm"], c.eps, out=xn)
             with T("gemm"):
-                lay["gate_up"](xn, out=gu)
+                r = lay["gate_up"](xn, out=gu, partials=fuse)
             with T("other"):
-                ops.silu_mul(gu, c.ffn, out=act)
+                if split(r):
+                    ops.splitk_silu_mul(r, c.ffn, out=act)
+                else:
+                    ops.silu_mul(gu, c.ffn, out=act)
             with T("gemm"):
-                lay["down"](act, out=h, residual=h if tp is None or tp.rank == 0 else None)
+                r = lay["down"](act, out=h, residual=h if tp is None or tp.rank == 0 else None, partials=fuse)
             if tp is not None:
                 with T("comm"):
                     self._all_reduce(h)
+            pending = r if split(r) else None
         with T("other"):
-            ops.rmsnorm(h, self.final_norm, c.eps, out=xn)
+            if pending is not None:
+                ops.splitk_rmsnorm(pending, self.final_norm, y=h, out=xn, residual=h, eps=c.eps)
+            else:
+                ops.rmsnorm(h, self.final_norm, c.eps, out=xn)
         if tp is None:
             with T("gemm"):
                 self.lm_head(xn, out=bf["logits"])

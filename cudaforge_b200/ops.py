@@ -118,3 +118,36 @@ def silu_mul(gu: torch.Tensor, ffn: int, out: Optional[torch.Tensor] = None, str
                                       _DT[gu.dtype], _s(stream, gu.device)), "cf_silu_mul")
     _lib.count()
     return out
+
+
+# ---- split-K consumers: `part` = (partials [S, M, N] fp32 view, S) from gemm.*_partials ----
+def splitk_rmsnorm(part, w: torch.Tensor, y: torch.Tensor, out: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                   eps: float = 1e-6, stream=None):
+    """y = reduce(partials) (+ residual), out = rmsnorm(y) * w (bit-identical to
+    the split-K reduction followed by rmsnorm)."""
+    p, S = part
+    M, N = y.shape
+    _lib.check(_lib.lib().cf_splitk_rmsnorm(p.data_ptr(), S, M, N, _ptr(residual),
+                                            residual.stride(0) if residual is not None else 0, y.data_ptr(),
+                                            y.stride(0), w.data_ptr(), out.data_ptr(), out.stride(0), eps,
+                                            _DT[y.dtype], _s(stream, y.device)), "cf_splitk_rmsnorm")
+    _lib.count()
+    return out
+
+
+def splitk_rope_qkv(part, qkv: torch.Tensor, pos: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                    k_new: torch.Tensor, v_new: torch.Tensor, base: float = 10000.0, stream=None) -> None:
+    p, S = part
+    _lib.check(_lib.lib().cf_splitk_rope_qkv(p.data_ptr(), S, qkv.shape[0], qkv.data_ptr(), qkv.stride(0),
+                                             num_q_heads, num_kv_heads, head_dim, pos.data_ptr(), base,
+                                             k_new.data_ptr(), v_new.data_ptr(), _DT[qkv.dtype],
+                                             _s(stream, qkv.device)), "cf_splitk_rope_qkv")
+    _lib.count()
+
+
+def splitk_silu_mul(part, ffn: int, out: torch.Tensor, stream=None):
+    p, S = part
+    _lib.check(_lib.lib().cf_splitk_silu_mul(p.data_ptr(), S, out.shape[0], ffn, out.data_ptr(), out.stride(0),
+                                             _DT[out.dtype], _s(stream, out.device)), "cf_splitk_silu_mul")
+    _lib.count()
+    return out

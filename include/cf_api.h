@@ -229,6 +229,18 @@ typedef struct cf_gemm_args {
 size_t cf_gemm_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t split_k, int32_t int4);
 int cf_w4a16_gemm(const cf_gemm_args *args, void *stream);
 int cf_dense_gemm(const cf_gemm_args *args, void *stream);
+/* Split-K without the reduction launch (no reference counterpart: the
+ * reference has no split-K).  cf_gemm_splits() = the number of K splits the
+ * plan for this shape uses (1 = no split, 0 = unsupported shape).  When it is
+ * > 1, the *_partials calls run only the GEMM and leave fp32 partials
+ * [splits][m][n] (contiguous) at the start of `workspace`, and `y` /
+ * `residual` are not touched; one of the cf_splitk_* consumers below then
+ * forms y exactly as the reduction would (fixed order s = 0..splits-1, then
+ * + residual, then one rounding) and fuses its own op.  With 1 split they
+ * behave as cf_w4a16_gemm / cf_dense_gemm. */
+int cf_gemm_splits(int32_t m, int32_t n, int32_t k, int32_t split_k, int32_t int4);
+int cf_w4a16_gemm_partials(const cf_gemm_args *args, void *stream);
+int cf_dense_gemm_partials(const cf_gemm_args *args, void *stream);
 /* Reference [k/8, n] packing -> kernel nibble order (same values). */
 int cf_w4a16_repack(const uint32_t *wq_ref, uint32_t *wq_out, int32_t k, int32_t n, void *stream);
 
@@ -413,6 +425,22 @@ int cf_rope_qkv(void *qkv, int64_t ld, int32_t m, int32_t num_q_heads, int32_t n
 /* SwiGLU: out[m, j] = silu(gu[m, j]) * gu[m, ffn + j] */
 int cf_silu_mul(const void *gu, int64_t ldg, void *out, int64_t ldo, int32_t m, int32_t ffn, int32_t dtype,
                 void *stream);
+
+/* Split-K consumers (partials from *_gemm_partials, m rows, n = row width):
+ * cf_splitk_rmsnorm: y = reduce(+ residual) written (in place over the
+ *   residual is allowed), out = RMSNorm(y) * w as cf_rmsnorm;
+ * cf_splitk_rope_qkv: cf_rope_qkv on the reduced QKV rows (n = (Hq + 2 Hkv)
+ *   * head_dim; rotated q is written to qkv, k / v to k_new / v_new);
+ * cf_splitk_silu_mul: cf_silu_mul on the reduced gate|up rows (n = 2 ffn).
+ * Bit-identical to the reduction followed by the plain op. */
+int cf_splitk_rmsnorm(const float *partials, int32_t splits, int32_t m, int32_t n, const void *residual,
+                      int64_t ldr, void *y, int64_t ldy, const void *w, void *out, int64_t ldo, float eps,
+                      int32_t dtype, void *stream);
+int cf_splitk_rope_qkv(const float *partials, int32_t splits, int32_t m, void *qkv, int64_t ld, int32_t num_q_heads,
+                       int32_t num_kv_heads, int32_t head_dim, const int32_t *pos, float base, void *k_new,
+                       void *v_new, int32_t dtype, void *stream);
+int cf_splitk_silu_mul(const float *partials, int32_t splits, int32_t m, int32_t ffn, void *out, int64_t ldo,
+                       int32_t dtype, void *stream);
 
 #ifdef __cplusplus
 }

@@ -107,3 +107,31 @@ def test_speculative_step_greedy_matches_target_argmax():
             seqs[b] = seqs[b] + emitted
         assert tr.committed == [len(x) - 1 for x in seqs]
     assert checked > 0
+
+
+@pytest.mark.parametrize("cfg,B", [(SMALL_INT4, 3), (LlamaConfig(1, 4096, 32, 8, 128, 14336, 4096), 64),
+                                   (TINY_TARGET, 3)], ids=["int4_small", "int4_8b_layer_m384", "tiny_fp16"])
+def test_fused_splitk_consumers_bit_identical(cfg, B):
+    """The split-K reductions fused into RoPE / residual+RMSNorm / SwiGLU give the
+    same bits as the reduction kernel followed by the plain ops."""
+    from cudaforge_b200 import _lib
+    model = LlamaModel(cfg, seed=4)
+    S0, K = 29, 5
+    runner = PagedRunner(model, model.make_cache(B * 4 + 8, max_batch=B), seq_ids=list(range(B)))
+    g = torch.Generator().manual_seed(6)
+    prompt = torch.randint(0, cfg.vocab, (B, S0), generator=g)
+    runner.prefill(prompt[:, :-1].tolist())
+    ids = torch.cat([prompt, torch.randint(0, cfg.vocab, (B, K), generator=g)], 1).cuda()
+    M = B * (K + 1)
+    from cudaforge_b200.gemm import MAX_FUSED_SPLITS
+    sp = [_lib.lib().cf_gemm_splits(M, n, k, 0, int(cfg.quant == "int4")) for _, n, k in cfg.linear_shapes()]
+    assert any(1 < x <= MAX_FUSED_SPLITS for x in sp), sp  # at least one fused split-K consumer runs
+    outs = []
+    for fuse in (False, True):
+        model.fuse_splitk = fuse
+        lg = runner.forward(ids).clone()
+        bf = model.buffers(B, K + 1)
+        outs.append((lg, bf["k_new"].clone(), bf["v_new"].clone()))
+    torch.cuda.synchronize()
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
