@@ -543,7 +543,8 @@ extern "C" int cf_dense_gemm(const cf_gemm_args *args, void *stream) {
 
 extern "C" int cf_gemm_splits(int32_t m, int32_t n, int32_t k, int32_t split_k, int32_t int4) {
   Plan pl;
-  if (m <= 0 || n <= 0 || k <= 0 || !make_plan(m, n, k, split_k, int4 != 0, pl)) return 0;
+  if (m <= 0 || n <= 0 || k <= 0 || n % HN != 0 || k % (int4 ? 128 : BK) != 0) return 0;  // as run_gemm
+  if (!make_plan(m, n, k, split_k, int4 != 0, pl)) return 0;
   return pl.splits;
 }
 

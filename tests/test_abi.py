@@ -38,3 +38,23 @@ def test_accept_tree_rejects_bad_args_on_host():
     assert L.cf_accept_tree(ctypes.byref(a), None) == _lib.CF_EINVAL
     a = _lib.CfAcceptTreeArgs(batch=0, nodes=3, vocab=10)
     assert L.cf_accept_tree(ctypes.byref(a), None) == _lib.CF_OK
+
+
+def test_gemm_plan_queries_on_host():
+    """Split-K plans of the benchmark shapes (148 SMs): the cfg3 qkv / o / down projections split
+    3-4 ways (fused consumers), gate_up and lm_head do not split; the draft's one-row steps split
+    up to 16 ways (reduction kernel).  Workspace = splits x M x N fp32 when split."""
+    from cudaforge_b200.gemm import MAX_FUSED_SPLITS
+    from cudaforge_b200.model import DRAFT_1B, LLAMA_8B
+    L = _lib.lib()
+    got = [L.cf_gemm_splits(384, n, k, 0, 1) for _, n, k in LLAMA_8B.linear_shapes()]
+    assert got == [3, 4, 1, 4]
+    assert L.cf_gemm_splits(384, LLAMA_8B.vocab, LLAMA_8B.d_model, 0, 1) == 1
+    assert all(1 < s <= MAX_FUSED_SPLITS for s in (got[0], got[1], got[3]))
+    for _, n, k in LLAMA_8B.linear_shapes():
+        s = L.cf_gemm_splits(384, n, k, 0, 1)
+        assert L.cf_gemm_workspace_bytes(384, n, k, 0, 1) == (s * 384 * n * 4 if s > 1 else 0)
+    draft = [L.cf_gemm_splits(64, n, k, 0, 1) for _, n, k in DRAFT_1B.linear_shapes()]
+    assert draft == [11, 16, 2, 16]
+    assert L.cf_gemm_splits(384, 6144, 4096, 1, 1) == 1       # split_k = 1 forces one piece
+    assert L.cf_gemm_splits(384, 100, 4096, 0, 1) == 0        # n % 128 != 0: unsupported
