@@ -132,31 +132,34 @@ def fill_random(cache, gen: torch.Generator) -> None:
             seg.copy_(torch.randn(seg.numel(), generator=gen, device=seg.device).to(seg.dtype))
 
 
-def setup(args, rank, device):
+def setup(args, rank, device, world=1):
     from cudaforge_b200.model import DRAFT_1B, LLAMA_8B, TINY_DRAFT, TINY_TARGET, LlamaModel
     from cudaforge_b200.runner import PagedRunner
     from cudaforge_b200.speculative import SpeculativeEngine
     from cudaforge_b200.verifier import BatchVerifier
 
+    from cudaforge_b200.shard import rank_sequence_ids
     tcfg, dcfg = (LLAMA_8B, DRAFT_1B) if args.config == "8b" else (TINY_TARGET, TINY_DRAFT)
     B, P, K = args.batch, args.ctx, args.k
-    steps_total = args.warmup + 2 * args.steps + 4
+    steps_total = args.warmup + 3 * args.steps + 8
     blocks_per_seq = math.ceil((P + steps_total * (K + 1)) / 16) + 2
-    target = LlamaModel(tcfg, device=device, seed=1000 + rank)
+    ids = rank_sequence_ids(rank, B)  # global sequence ids of this rank's shard
+    # every rank holds a replica of the same weights; the prompts are this rank's rows of one global set
+    target = LlamaModel(tcfg, device=device, seed=1000)
     cache = target.make_cache(B * blocks_per_seq + 8, max_batch=B, max_blocks_per_seq=blocks_per_seq + 4)
-    ver = BatchVerifier(target, cache, list(range(B)), K, temperature=args.temperature,
+    ver = BatchVerifier(target, cache, ids, K, temperature=args.temperature,
                         max_blocks_per_seq=blocks_per_seq + 4, use_graph=not args.no_graph)
-    g = torch.Generator().manual_seed(7 + rank)
-    prompts = torch.randint(0, tcfg.vocab, (B, P), generator=g)
+    g = torch.Generator().manual_seed(7)
+    prompts = torch.randint(0, tcfg.vocab, (B * world, P), generator=g)[ids[0]: ids[-1] + 1]
     ver.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
     gd = torch.Generator(device=device).manual_seed(11 + rank)
     ver.fill_synthetic_kv(gd)
     # draft: the 1B-shaped INT4 model proposes K tokens per sequence through the device-resident
     # draft loop (its first round gives the drafts the verify steps reuse; rounds are timed separately)
     from cudaforge_b200.drafter import BatchDrafter
-    draft = LlamaModel(dcfg, device=device, seed=2000 + rank)
+    draft = LlamaModel(dcfg, device=device, seed=2000)
     dcache = draft.make_cache(B * blocks_per_seq + 8, max_batch=B, max_blocks_per_seq=blocks_per_seq + 4)
-    drafter = BatchDrafter(draft, dcache, list(range(B)), K, temperature=args.temperature,
+    drafter = BatchDrafter(draft, dcache, ids, K, temperature=args.temperature,
                            max_blocks_per_seq=blocks_per_seq + 4, use_graph=not args.no_graph)
     drafter.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
     fill_random(dcache, gd)
@@ -255,7 +258,7 @@ def run_ours(args):
     elif tree:
         tcfg, target, cache, ver, dtok, dlog = setup_tree(args, rank, device)
     else:
-        tcfg, target, cache, ver, dtok, dlog, drafter = setup(args, rank, device)
+        tcfg, target, cache, ver, dtok, dlog, drafter = setup(args, rank, device, world)
     B = args.batch
     R = dlog.shape[1] if tree else args.k + 1
     K = R - 1
@@ -280,24 +283,31 @@ def run_ours(args):
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     e0.record()
+    step_ev[0].record()
     for i in range(args.steps):
         res = ver.step(dtok, dlog, uni[args.warmup + i])
+        step_ev[i + 1].record()
         tokens_per_step.append(int((ver.n_pinned.clamp_min(0) + 1).sum()))
     e1.record()
     barrier()
+    ver.check_status()  # a timed-out wait or a bad page id voids the measurement
     launches = _lib.LAUNCHES[0] - l0
     ms = e0.elapsed_time(e1)
-    # ---- per-kernel timing pass (same step, CUDA events around every launch group) ----
+    step_ms = sorted(step_ev[i].elapsed_time(step_ev[i + 1]) for i in range(args.steps))
+    # ---- per-kernel timing pass: the same step launched eagerly with CUDA events around every
+    # launch group; a device-side sleep queued first keeps the GPU busy while the host enqueues
+    # the step, so each event pair brackets device time only (no host launch gaps) ----
     kt = KernelTimer()
     kp = max(2, min(args.steps, 4))
-    kstart = torch.cuda.Event(enable_timing=True)
-    kend = torch.cuda.Event(enable_timing=True)
-    kstart.record()
+    ctx_sums = []
     for i in range(kp):
+        ctx_sums.append(sum(ver.ctx_host))  # context of the step's attention (before its commit)
+        torch.cuda._sleep(60_000_000)  # ~30 ms of device time at 1.9 GHz
         ver.step(dtok, dlog, uni[total_steps + i], timer=kt)
-    kend.record()
     torch.cuda.synchronize(device)
+    ver.check_status()
     # ---- e2e: host inputs (pinned) -> device, results -> host, every step ----
     h_tok = dtok.cpu().pin_memory()
     h_uni = uni[total_steps: total_steps + args.steps].cpu().pin_memory()
@@ -320,7 +330,13 @@ def run_ours(args):
         e2e_tokens += int((h_out_n.clamp_min(0) + 1).sum())
     x1.record()
     barrier()
+    ver.check_status()
     e2e_ms = x0.elapsed_time(x1)
+    # the host gathers every rank's emitted tokens of the last e2e step (outside the timed regions)
+    from cudaforge_b200.shard import gather_emitted
+    nl = h_out_n.tolist()
+    gathered = gather_emitted(ver.seq_ids, [h_out_tok[b, : max(0, nl[b]) + 1].tolist() for b in range(B)]) \
+        if not tp else None
     h2d = dtok.numel() * 4 + B * R * 4
     d2h = B * R * 4 + B * 4
 
@@ -348,6 +364,8 @@ def run_ours(args):
             drafter.advance(r, n_host)
         r1.record()
         barrier()
+        ver.check_status()
+        drafter.st.sync_check("BatchDrafter")
         round_ms = r0.elapsed_time(r1)
         draft_ms = sum(a.elapsed_time(b) for a, b in d_ev)
         round_info = [round_ms, draft_ms, float(round_tokens)]
@@ -374,16 +392,27 @@ def run_ours(args):
     peaks, peak_src = load_peaks()
     M = B * R
     gemm_flops = tcfg.gemm_flops(M) / (world if tp else 1)  # per rank
-    gemm_ms = kt.total_ms("gemm") / kp
-    attn_ms = kt.total_ms("attn") / kp
-    other_ms = kt.total_ms("other") / kp
-    step_ms_k = kstart.elapsed_time(kend) / kp
+    kms = {k: kt.total_ms(k) / kp for k in ("gemm", "attn", "accept", "commit", "other", "comm")}
+    gemm_ms, attn_ms = kms["gemm"], kms["attn"]
     achieved_tf = gemm_flops / (gemm_ms / 1e3) / 1e12
-    peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
-    ctx_mean = statistics.mean(ver.ctx_host)
-    attn_bytes = tcfg.layers * B * (ctx_mean + R) * target.lcfg.n_kv_heads * tcfg.head_dim * 2 * 2  # per rank
+    # burst peak for kernels that ran at the maximum SM clock (a short timed window), the
+    # sustained (power-capped) one when the clocks show the cap
+    at_max = (clocks.get("sm_mhz") or 0) >= 0.97 * (clocks.get("sm_max_mhz") or 1) \
+        and "sw_power_cap" not in clocks.get("reasons", [])
+    peak_key = "bf16_tflops" if at_max else "bf16_tflops_sustained"
+    peak_tf = float(peaks.get(peak_key, FALLBACK_PEAKS[peak_key]))
+    lc = target.lcfg
+    # attention reads every context token's K and V of every layer once, plus the new rows
+    ctx_mean_sum = statistics.mean(ctx_sums)
+    attn_bytes = tcfg.layers * (ctx_mean_sum + B * R) * lc.n_kv_heads * tcfg.head_dim * 2 * 2  # per rank
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
-    # DRAM bytes of the step's GEMMs from the committed ncu summary (cfg3 shapes only)
+    elem = 2  # bf16 logits
+    acc_rows = (tree and 2 * R or 2 * K + 1)
+    acc_bytes = B * acc_rows * tcfg.vocab * elem
+    commit_bytes = statistics.mean(tokens_per_step) * tcfg.layers * lc.n_kv_heads \
+        * tcfg.head_dim * 2 * 2 * 2  # K and V rows, read from scratch + written to the pool
+    # DRAM bytes of the step's GEMM launches as captured by ncu at the cfg3 shapes (B=64, K=5):
+    # a committed profile figure, not measured by this run
     traffic = None
     tr_path = os.path.join(ROOT, "profiles", "w4a16_gemm_traffic_cfg3.md")
     if not tree and not tp and B == 64 and K == 5 and os.path.exists(tr_path):
@@ -391,12 +420,20 @@ def run_ours(args):
         m = re.search(r"traffic_bytes_per_step:\s*(\d+)", open(tr_path).read())
         traffic = int(m.group(1)) if m else None
 
+    def hbm_entry(byts, ms_):
+        if not ms_:
+            return None
+        gbs = byts / (ms_ / 1e3) / 1e9
+        return {"bound": "hbm", "bytes_per_step": round(byts), "ms_per_step": round(ms_, 4),
+                "achieved_gbs": round(gbs, 1), "peak_gbs": hbm, "frac": round(gbs / hbm, 4),
+                "peak_source": f"{peak_src} hbm_gbs"}
+
     out = None
     if rank == 0:
         out = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
-            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if (tp or args.global_batch) else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: random-init weights (INT4 uniform [-8,7], |N(0,0.002)| fp16 scales), random "
                     "prompt ids, context K/V seeded random (stands in for a prefill), drafts from the random-init "
                     "1B INT4 draft model",
@@ -407,15 +444,22 @@ def run_ours(args):
                        "draft": ("8B-shaped W4A16 replicated per rank" if tp else "1B-shaped W4A16")
                                 + " (excluded from timing)",
                        "global_batch": B if tp else B * world,
+                       **({"sequences_gathered_on_rank0": len(gathered)} if gathered is not None else {}),
                        "batch_per_gpu": B, "seq_len": args.ctx, **({"tree_nodes": K} if tree else {"k": K}),
                        "temperature": args.temperature,
                        "parallelism": (f"tensor-parallel tp{world} (NCCL all-reduce after O and down, "
                                        "all-gather of the vocabulary shards)" if tp
-                                       else f"batch-sharded dp{world} (no collective)"),
+                                       else f"batch-sharded dp{world} (no collective; "
+                                       + ("fixed global batch split over the ranks" if args.global_batch
+                                          else "fixed batch per GPU") + ")"),
                        "l2": "inputs larger than L2 (GB-sized INT4 weights + KV pools per GPU)",
                        "mean_accepted_per_seq_step": round(tok_all / (args.steps * B * (1 if tp else world)) - 1, 3)},
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
+            "verify_latency_ms": {"p50": round(statistics.median(step_ms), 3),
+                                  "p95": round(step_ms[min(len(step_ms) - 1, math.ceil(0.95 * len(step_ms)) - 1)], 3),
+                                  "min": round(step_ms[0], 3), "max": round(step_ms[-1], 3),
+                                  "what": "per-step CUDA-event time of the headline loop (rank 0)"},
             "gpu_launches": launches,
             **({"speculative_round": round_out} if round_out else {}),
             "clocks": clocks,
@@ -423,18 +467,25 @@ def run_ours(args):
                                    + (", per rank)" if tp else ")"),
                          "achieved": round(achieved_tf, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(achieved_tf / peak_tf, 4), "traffic": traffic,
-                         "traffic_scope": "DRAM bytes of the step's GEMM launches (ncu, profiles/w4a16_gemm_traffic_cfg3.md)",
-                         "peak_source": f"{peak_src} bf16_tflops_sustained",
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the step's GEMM "
+                                           "launches at B=64, K=5 (profiles/w4a16_gemm_traffic_cfg3.md); a committed "
+                                           "profile figure, not measured by this run",
+                         "algorithmic_bytes_per_step": round(tcfg.weight_bytes() / (world if tp else 1)
+                                                             + 2 * M * sum(n + k for _, n, k in lc.linear_shapes())
+                                                             * tcfg.layers),
+                         "peak_source": f"{peak_src} {peak_key} (burst when the timed window ran at max SM clock "
+                                        "without a power cap, else sustained)",
                          "algorithmic_flops_per_step": gemm_flops, "gemm_ms_per_step": round(gemm_ms, 3),
                          "splitk_reduction": "fused into the consuming RoPE / residual+RMSNorm / SwiGLU launches "
                                              "(timed under kernels.other_ms, not in gemm_ms)"},
             "kernels": {
-                "step_ms_instrumented": round(step_ms_k, 3),
-                "gemm_ms": round(gemm_ms, 3), "attn_ms": round(attn_ms, 3), "other_ms": round(other_ms, 3),
-                **({"comm_ms": round(kt.total_ms("comm") / kp, 3)} if tp else {}),
-                "attention": {"bound": "hbm", "bytes_per_step": attn_bytes,
-                              "achieved_gbs": round(attn_bytes / (attn_ms / 1e3) / 1e9, 1),
-                              "peak_gbs": hbm, "frac": round(attn_bytes / (attn_ms / 1e3) / 1e9 / hbm, 4)},
+                "timing": "eager instrumented pass: CUDA events around each launch group, the GPU kept ahead of "
+                          "the host (device-side sleep queued first), so the sums are device time",
+                "step_ms_instrumented": round(sum(kms.values()), 3),
+                **{f"{k}_ms": round(v, 3) for k, v in kms.items() if v or k != "comm"},
+                "attention": hbm_entry(attn_bytes, attn_ms),
+                "acceptance": hbm_entry(acc_bytes, kms["accept"]),
+                "kv_commit": hbm_entry(commit_bytes, kms["commit"]),
             },
         }
     if world > 1:
@@ -648,7 +699,9 @@ def main():
     ap.add_argument("--config", default="8b", choices=["8b", "tiny", "8b-tree", "70b-tp"],
                     help="8b = cfg3 chain (default); 8b-tree = cfg4 (B=32, 4096 context, 64-node tree); "
                          "70b-tp = cfg5 (70B tensor-parallel over the ranks, B=128, 2048 context, K=4)")
-    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (weak scaling)")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="fixed global batch split evenly over the GPUs (strong scaling), e.g. 64 -> 32/16/8 per GPU")
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--k", type=int, default=5)
     ap.add_argument("--temperature", type=float, default=1.0)
@@ -659,6 +712,9 @@ def main():
     ap.add_argument("--shape", default=None, help="NxK for --case gemm")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
+    if args.global_batch is not None:
+        from cudaforge_b200.shard import split_global_batch
+        args.batch = split_global_batch(args.global_batch, int(os.environ.get("WORLD_SIZE", "1")))
     if args.batch is None:
         args.batch = {"8b-tree": 32, "70b-tp": 128}.get(args.config, 64)
     if args.ctx is None:

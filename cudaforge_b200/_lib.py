@@ -155,3 +155,40 @@ def declared_symbols() -> list[str]:
             src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
             names += re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\**\s*(cf_[a-z0-9_]+)\s*\(", src, flags=re.M)
     return names
+
+
+class DeviceError(RuntimeError):
+    """A kernel recorded a non-zero status word on the device (CF_ETIMEOUT for a
+    bounded wait that ran out, CF_ERANGE for an out-of-range page or row id)."""
+
+    def __init__(self, code: int, where: str):
+        self.code = code
+        super().__init__(f"{where}: device status {code} ({lib().cf_status_string(code).decode()})")
+
+
+class DeviceStatus:
+    """The int32 status word the kernels of one step write on the device, with
+    a pinned host mirror.  snapshot() enqueues the copy on the current stream;
+    after that stream has been synchronised, check() raises DeviceError on any
+    non-zero code and clears the word for the next step."""
+
+    def __init__(self, device):
+        import torch
+        self.dev = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    def snapshot(self) -> None:
+        self.host.copy_(self.dev, non_blocking=True)
+
+    def check(self, where: str) -> None:
+        code = int(self.host[0])
+        if code != CF_OK:
+            self.dev.zero_()
+            self.host.zero_()
+            raise DeviceError(code, where)
+
+    def sync_check(self, where: str) -> None:
+        import torch
+        self.snapshot()
+        torch.cuda.current_stream(self.dev.device).synchronize()
+        self.check(where)

@@ -471,8 +471,6 @@ __global__ void attn_combine_kernel(const AttnParams p) {
 // Row tiles of 16 query rows per page stream: 1 when a kv-head group's rows fit
 // in 16 (decode-like steps: fewer idle MMA rows, up to three CTAs per SM), else 2.
 int attn_mt(int rows_total) {
-  const char *v = getenv("CF_ATTN_MT");
-  if (v && atoi(v) > 0) return atoi(v) == 1 ? 1 : 2;
   return rows_total <= 16 ? 1 : 2;
 }
 

@@ -30,7 +30,7 @@ __global__ void kv_commit_kernel(const cf_kv_commit_args a) {
     const int src_row = a.row_index ? a.row_index[(int64_t)b * a.rows + j] : j;
     const int pos = start + j;
     const int page = pos / bs, slot = pos % bs;
-    const int blk = (page < a.max_blocks) ? a.block_tables[(int64_t)b * a.max_blocks + page] : -1;
+    const int blk = (pos >= 0 && page < a.max_blocks) ? a.block_tables[(int64_t)b * a.max_blocks + page] : -1;
     if (blk < 0 || blk >= a.kv.total_blocks || src_row < 0 || src_row >= a.rows) {
       if (a.status) atomicExch(a.status, CF_ERANGE);
       continue;

@@ -79,8 +79,15 @@ struct GemmParams {
 // holds k = 2p for p < 4 and k = 2(p-4)+1 for p >= 4, so masking with
 // 0x000F000F after shifts of 0/4/8/12 yields the pairs (k0,k1) (k2,k3)
 // (k4,k5) (k6,k7).  OR-ing 0x4300 builds bf16 128 + nibble exactly;
-// subtracting 136 gives nibble - 8 exactly; one bf16 multiply by the scale.
-__device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 s2) {
+// subtracting 136 gives v = nibble - 8 exactly.
+// The weight is bf16(v * s) with ONE rounding of the exact product, as the
+// reference dequantises in fp32 and then casts to the activation type
+// (csrc/kernels/triton/int4_dequant_triton.py:66).  The fp16 scale s (11
+// significant bits) is split as s = s_hi + s_lo with s_hi = bf16(s) and s_lo
+// = s - s_hi (at most 3 significant bits, exact in bf16); v * s_lo has at most
+// 6 significant bits and is exact in bf16, so fma(v, s_hi, v * s_lo) rounds
+// v * s exactly once.
+__device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 s_hi, __nv_bfloat162 s_lo) {
   const uint32_t kMask = 0x000F000Fu, kMagic = 0x43004300u;
   const __nv_bfloat162 k136 = __floats2bfloat162_rn(136.0f, 136.0f);
   uint32_t h[4] = {(w & kMask) | kMagic, ((w >> 4) & kMask) | kMagic, ((w >> 8) & kMask) | kMagic,
@@ -90,7 +97,8 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 s2) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162 *>(&h[j]);
-    v = __hmul2(__hsub2(v, k136), s2);
+    v = __hsub2(v, k136);
+    v = __hfma2(v, s_hi, __hmul2_rn(v, s_lo));
     op[j] = *reinterpret_cast<uint32_t *>(&v);
   }
   return o;
@@ -136,7 +144,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
 #define CF_TRACE(role, i) \
   if (tr && (i) < 512) p.trace[(role) * 512 + (i)] = clock64()
 
+  // set when any role's bounded wait ran out: every role then drains before TMEM is freed
+  volatile int &s_fail = *reinterpret_cast<volatile int *>(tmem_slot + 1);
   if (threadIdx.x == 0) {
+    s_fail = 0;
     for (int s = 0; s < SW; ++s) { mbar_init(&wfull[s], 1); mbar_init(&wempty[s], 8); }
     for (int s = 0; s < SX; ++s) { mbar_init(&xfull[s], 1); mbar_init(&xempty[s], 1); }
     for (int s = 0; s < SA; ++s) { mbar_init(&afull[s], WM == kInt4 ? 8 : 1); mbar_init(&aempty[s], 1); }
@@ -154,13 +165,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
+  int issued_w = 0, issued_x = 0;  // copies this CTA's producers started (drained on failure)
 
   if (warp == 0) {
     // ---------------- weight producer ----------------
     const int S = WM == kInt4 ? SW : SA;
     uint64_t *fullb = WM == kInt4 ? wfull : afull;
     uint64_t *emptyb = WM == kInt4 ? wempty : aempty;
-    int issued = 0;
     for (int i = 0; i < nkb; ++i) {
       const int s = i % S;
       const uint32_t ph = (uint32_t)(i / S) & 1u;
@@ -184,14 +195,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
                       n0 + (lane - l0) * HN);
       }
       __syncwarp();
-      issued = i + 1;
+      issued_w = i + 1;
     }
-    if (!ok)  // let our own copies land before the CTA can exit
-      for (int j = max(0, issued - S); j < issued; ++j)
-        mbar_wait_warp(&fullb[j % S], (uint32_t)(j / S) & 1u, kDrainNs);
   } else if (warp == 10) {
     // ---------------- token-tile producer ----------------
-    int issued = 0;
     for (int i = 0; i < nkb; ++i) {
       const int s = i % SX;
       const uint32_t ph = (uint32_t)(i / SX) & 1u;
@@ -211,11 +218,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
           tma_load_2d(x_ring + s * p.x_bytes + b * 2048, &tm_x, &xfull[s], kb * BK, m0 + b * 16);
       }
       __syncwarp();
-      issued = i + 1;
+      issued_x = i + 1;
     }
-    if (!ok)
-      for (int j = max(0, issued - SX); j < issued; ++j)
-        mbar_wait_warp(&xfull[j % SX], (uint32_t)(j / SX) & 1u, kDrainNs);
   } else if (warp == 1) {
     // ---------------- MMA issue: the whole warp walks the loop, one elected lane issues ----------------
     const uint32_t idesc = p.idesc;
@@ -262,22 +266,24 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     if (WM == kInt4) {
       for (int i = 0; i < nkb; ++i) {
         const int sw = i % SW, sa = i % SA;
-        if (!mbar_wait(&wfull[sw], (uint32_t)(i / SW) & 1u, p.timeout_ns)) { ok = false; break; }
+        // warp-uniform waits: a lane must not leave the loop while the others reach __syncwarp
+        if (!mbar_wait_warp(&wfull[sw], (uint32_t)(i / SW) & 1u, p.timeout_ns)) { ok = false; break; }
         const uint8_t *st = w_ring + sw * kWStageBytes;
         const uint32_t *wp = reinterpret_cast<const uint32_t *>(st);
-        const __nv_bfloat16 sb =
-            __float2bfloat16_rn(__half2float(reinterpret_cast<const __half *>(st + kWPackBytes)[t]));
-        const __nv_bfloat162 s2 = __halves2bfloat162(sb, sb);
+        const float sf = __half2float(reinterpret_cast<const __half *>(st + kWPackBytes)[t]);
+        const __nv_bfloat16 sh = __float2bfloat16_rn(sf);
+        const __nv_bfloat16 sl = __float2bfloat16_rn(sf - __bfloat162float(sh));  // exact remainder
+        const __nv_bfloat162 s_hi = __halves2bfloat162(sh, sh), s_lo = __halves2bfloat162(sl, sl);
         uint32_t a[32];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint4 v = dequant8(wp[kk * TN + t], s2);
+          const uint4 v = dequant8(wp[kk * TN + t], s_hi, s_lo);
           a[4 * kk + 0] = v.x; a[4 * kk + 1] = v.y; a[4 * kk + 2] = v.z; a[4 * kk + 3] = v.w;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&wempty[sw]);  // packed words are consumed
         // dequantised into registers first: only the TMEM store waits for the A slot
-        if (i >= SA && !mbar_wait(&aempty[sa], ((uint32_t)(i / SA) & 1u) ^ 1u, p.timeout_ns)) { ok = false; break; }
+        if (i >= SA && !mbar_wait_warp(&aempty[sa], ((uint32_t)(i / SA) & 1u) ^ 1u, p.timeout_ns)) { ok = false; break; }
         tc_fence_after();
         if (threadIdx.x == 64) CF_TRACE(1, i);
         if (h < halves)
@@ -290,7 +296,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       }
     }
     // ---------------- epilogue ----------------
-    if (!mbar_wait(accf, 0, ok ? p.timeout_ns : kDrainNs)) ok = false;
+    if (!mbar_wait_warp(accf, 0, ok ? p.timeout_ns : kDrainNs)) ok = false;
     tc_fence_after();
     if (threadIdx.x == 64) CF_TRACE(5, 0);
     if (ok) {
@@ -340,7 +346,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       }
     }
   }
-  if (!ok && p.status) atomicExch(p.status, CF_ETIMEOUT);
+  if (!ok) s_fail = 1;
+  __syncthreads();
+  if (s_fail) {
+    // Some wait ran out, so other roles may have stopped early: before the CTA can
+    // exit, let this CTA's own TMA copies land and every MMA it issued finish
+    // (all bounded), then free TMEM.
+    if (warp == 0) {
+      const int S = WM == kInt4 ? SW : SA;
+      uint64_t *fullb = WM == kInt4 ? wfull : afull;
+      for (int j = max(0, issued_w - S); j < issued_w; ++j)
+        mbar_wait_warp(&fullb[j % S], (uint32_t)(j / S) & 1u, kDrainNs);
+    } else if (warp == 10) {
+      for (int j = max(0, issued_x - SX); j < issued_x; ++j)
+        mbar_wait_warp(&xfull[j % SX], (uint32_t)(j / SX) & 1u, kDrainNs);
+    } else if (warp == 1) {
+      mbar_wait_warp(accf, 0, kDrainNs);
+    }
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, CF_ETIMEOUT);
+  }
   if (threadIdx.x == 64) CF_TRACE(5, 1);
   tc_fence_before();
   __syncthreads();
@@ -406,8 +430,7 @@ int num_sms() {
 
 bool make_plan(int M, int N, int K, int split_req, bool int4, Plan &pl) {
   // INT4: TMEM = two accumulators (2 x m_slice columns) + >= 2 dequantised-A stages (64 columns each)
-  auto env0 = [](const char *n, int d) { const char *v = getenv(n); return v ? atoi(v) : d; };
-  const int max_slice = int4 ? env0("CF_GEMM_MAXSLICE", 192) : kMaxSlice;
+  const int max_slice = int4 ? 192 : kMaxSlice;
   pl.slices = (M + max_slice - 1) / max_slice;
   const int per = (M + pl.slices - 1) / pl.slices;
   pl.m_slice = (per + 15) / 16 * 16;  // loaded as m_slice/16 boxes of 16 rows
@@ -416,18 +439,17 @@ bool make_plan(int M, int N, int K, int split_req, bool int4, Plan &pl) {
   pl.x_bytes = (uint32_t)pl.m_slice * 128u;
   const size_t budget = kMaxSmem - 1024 - 1024;  // alignment slack + barriers
   const size_t w_stage = int4 ? kWStageBytes : 0;
-  auto env = [](const char *n, int d) { const char *v = getenv(n); return v ? atoi(v) : d; };
   if (int4) {
     pl.a_tcol = (2u * pl.m_slice + 31u) & ~31u;
-    pl.sa = std::min(env("CF_GEMM_SA", 4), (int)((512u - pl.a_tcol) / 64u));
+    pl.sa = std::min(4, (int)((512u - pl.a_tcol) / 64u));
     pl.tmem_cols = 512;
   } else {
     pl.a_tcol = 0;
-    pl.sa = env("CF_GEMM_SA", 3);
+    pl.sa = 3;
   }
   const size_t a_bytes = int4 ? (size_t)kAStageBytes : pl.sa * (size_t)kAStageBytes;
-  pl.sw = int4 ? env("CF_GEMM_SW", 8) : 1;
-  pl.sx = (int)std::min<size_t>(env("CF_GEMM_SX", 6), (budget - a_bytes - pl.sw * w_stage) / pl.x_bytes);
+  pl.sw = int4 ? 8 : 1;
+  pl.sx = (int)std::min<size_t>(6, (budget - a_bytes - pl.sw * w_stage) / pl.x_bytes);
   if (pl.sx < 2 && !int4) { pl.sa = 2; pl.sx = (int)std::min<size_t>(4, (budget - 2 * (size_t)kAStageBytes) / pl.x_bytes); }
   if (pl.sx < 2 || pl.sa < 2 || (int4 && pl.sw < 2)) return false;
   pl.off_x = (uint32_t)(int4 ? kAStageBytes : pl.sa * kAStageBytes);

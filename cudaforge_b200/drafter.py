@@ -66,7 +66,9 @@ class BatchDrafter:
                                 num_accepted=torch.zeros(B, dtype=torch.int32, device=dev),
                                 eos=torch.zeros(B, dtype=torch.bool, device=dev))
         self.ws = torch.empty(4096 + 16 * B, dtype=torch.uint8, device=dev)
-        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        from . import _lib
+        self.st = _lib.DeviceStatus(dev)
+        self.status = self.st.dev
         self.cap = max_blocks_per_seq
         self.tables_pinned = torch.full((B * max_blocks_per_seq,), -1, dtype=torch.int32).pin_memory()
         self.ctx_pinned = torch.zeros(B, dtype=torch.int32).pin_memory()
@@ -160,11 +162,12 @@ class BatchDrafter:
             _lib.count(self.kernels_per_round)
         elif self.use_graph and self.calls >= 1:
             from . import gemm as _gemm
-            self._keep = [dict(ops._Ws.bufs), dict(_gemm._Ws.bufs)]  # workspaces the graph addresses
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 self._round(self.cap * self.cache.get_config().block_size)
             self.graph = g
+            # workspaces the graph addresses, taken after capture (a capture can grow them)
+            self._keep = [dict(ops._Ws.bufs), dict(_gemm._Ws.bufs)]
             _lib.LAUNCHES[0] = l0  # capture records launches without running them
             g.replay()
             _lib.count(self.kernels_per_round)
@@ -172,6 +175,7 @@ class BatchDrafter:
             self._round(max(self.base_host) + self.K)
             self.kernels_per_round = _lib.LAUNCHES[0] - l0
         self.calls += 1
+        self.st.snapshot()  # checked by advance(), after the verifier's step has synchronised the stream
         return self.tokens, self.logits
 
     @torch.no_grad()
@@ -182,6 +186,7 @@ class BatchDrafter:
         already needed).  Grows the draft tables by n + 1 tokens per sequence
         and moves (P-1, P) to the last two emitted tokens."""
         B = self.B
+        self.st.check("BatchDrafter.draft")
         ext = torch.cat([self.last.view(B, 1), res.tokens], 1)   # ext[b, i + 1] = emitted token i
         n = res.num_accepted.clamp_min(0).long().view(B, 1)
         self.prev.copy_(ext.gather(1, n).view(B))                # emitted token n-1 (old last when n = 0)

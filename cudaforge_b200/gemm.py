@@ -80,7 +80,9 @@ def _gemm(fn, x, w, scales, n, residual, out, split_k, workspace, status, int4, 
     if fused:
         fn = partials_fn
     need = L.cf_gemm_workspace_bytes(M, n, K, split_k, int(int4))
-    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+    if workspace is not None and workspace.dtype != torch.uint8:
+        raise ValueError("workspace must be a uint8 (byte) tensor")
+    if need and (workspace is None or workspace.numel() < need):
         workspace = _Ws.get(x.device, need)
     a = _lib.CfGemmArgs(m=M, n=n, k=K, act_dtype=_DT[x.dtype], x=x.data_ptr(), ldx=x.stride(0),
                         w=w.data_ptr(), scales=scales.data_ptr() if scales is not None else None,
@@ -106,7 +108,9 @@ def w4a16_gemm(x: torch.Tensor, wq_kernel: torch.Tensor, scales: torch.Tensor, *
     """y = x @ deq(W) (+ residual); x bf16 [M, K], wq_kernel from repack_int4, scales fp16 [K/128, N].
     partials=True: when the plan splits K into 2..MAX_FUSED_SPLITS pieces, run only the GEMM
     and return (fp32 partials [splits, M, N] in the workspace, splits) for an ops.splitk_*
-    consumer (residual and out untouched); otherwise y as usual."""
+    consumer (residual and out untouched); otherwise y as usual.  Without a caller
+    workspace the partials live in a per-device buffer shared by every GEMM: they are
+    valid only until the next GEMM call on that device is enqueued."""
     n = wq_kernel.shape[1]
     L = _lib.lib()
     return _gemm(L.cf_w4a16_gemm, x, wq_kernel, scales, n, residual, out, split_k, workspace, status,

@@ -110,13 +110,14 @@ class Linear:
             return Linear._wrap("int4", self.n, k1 - k0, wq=self.wq[k0 // 8: k1 // 8], scales=self.scales[k0 // 128: k1 // 128])
         return Linear._wrap(self.quant, self.n, k1 - k0, w=self.w[:, k0:k1])
 
-    def __call__(self, x, out=None, residual=None, workspace=None, partials=False):
+    def __call__(self, x, out=None, residual=None, workspace=None, partials=False, status=None):
         """y = x W^T (+ residual) into `out`; with partials=True a K-split plan returns
         (fp32 partials, splits) for an ops.splitk_* consumer instead (out untouched)."""
         if self.quant == "int4":
             return w4a16_gemm(x, self.wq, self.scales, out=out, residual=residual, workspace=workspace,
-                              partials=partials)
-        return dense_gemm(x, self.w, out=out, residual=residual, workspace=workspace, partials=partials)
+                              partials=partials, status=status)
+        return dense_gemm(x, self.w, out=out, residual=residual, workspace=workspace, partials=partials,
+                          status=status)
 
 
 @dataclasses.dataclass(frozen=True)
@@ -281,7 +282,7 @@ class LlamaModel:
                 else:
                     ops.rmsnorm(h, lay["attn_norm"], c.eps, out=xn)
             with T("gemm"):
-                r = lay["qkv"](xn, out=qkv, partials=fuse)
+                r = lay["qkv"](xn, out=qkv, partials=fuse, status=status)
             with T("other"):
                 if split(r):
                     ops.splitk_rope_qkv(r, qkv, positions, c.n_heads, c.n_kv_heads, c.head_dim, bf["k_new"][li],
@@ -294,7 +295,8 @@ class LlamaModel:
                                      max_context, rows=R, num_q_heads=c.n_heads, out=attn, tree_mask=tree_mask,
                                      status=status)
             with T("gemm"):  # TP: rank 0 carries the residual, the all-reduce sums the partial outputs
-                r = lay["o"](attn, out=h, residual=h if tp is None or tp.rank == 0 else None, partials=fuse)
+                r = lay["o"](attn, out=h, residual=h if tp is None or tp.rank == 0 else None, partials=fuse,
+                               status=status)
             if tp is not None:
                 with T("comm"):
                     self._all_reduce(h)
@@ -304,14 +306,15 @@ class LlamaModel:
                 else:
                     ops.rmsnorm(h, lay["ffn_norm"], c.eps, out=xn)
             with T("gemm"):
-                r = lay["gate_up"](xn, out=gu, partials=fuse)
+                r = lay["gate_up"](xn, out=gu, partials=fuse, status=status)
             with T("other"):
                 if split(r):
                     ops.splitk_silu_mul(r, c.ffn, out=act)
                 else:
                     ops.silu_mul(gu, c.ffn, out=act)
             with T("gemm"):
-                r = lay["down"](act, out=h, residual=h if tp is None or tp.rank == 0 else None, partials=fuse)
+                r = lay["down"](act, out=h, residual=h if tp is None or tp.rank == 0 else None, partials=fuse,
+                                  status=status)
             if tp is not None:
                 with T("comm"):
                     self._all_reduce(h)
@@ -323,11 +326,11 @@ class LlamaModel:
                 ops.rmsnorm(h, self.final_norm, c.eps, out=xn)
         if tp is None:
             with T("gemm"):
-                self.lm_head(xn, out=bf["logits"])
+                self.lm_head(xn, out=bf["logits"], status=status)
             return bf["logits"]
         import torch.distributed as dist
         with T("gemm"):
-            self.lm_head(xn, out=bf["logits_local"])
+            self.lm_head(xn, out=bf["logits_local"], status=status)
         with T("comm"):
             dist.all_gather_into_tensor(bf["logits_gather"], bf["logits_local"], group=tp.group)
             v = c.vocab  # this rank's true vocabulary slice (the shard is padded to 128 columns)

@@ -44,10 +44,12 @@ def verify_attention(cache, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_
                      block_tables: torch.Tensor, context_lens: torch.Tensor, max_context: int, *,
                      rows: int, num_q_heads: int, out: Optional[torch.Tensor] = None,
                      tree_mask: Optional[torch.Tensor] = None, num_splits: int = 0, status=None,
-                     new_kv_all_layers: bool = False, stream=None, trace=None) -> torch.Tensor:
+                     new_kv_all_layers: bool = False, stream=None, trace=None, timeout_ns: int = 0) -> torch.Tensor:
     """q [B*R, Hq*D] (row pitch q.stride(0)); k_new/v_new [B, R, Hkv, D] (or
     [L, B, R, Hkv, D] with new_kv_all_layers); block_tables [B, max_blocks]
-    int32; context_lens [B] int32; tree_mask [B, R, W] int64 bit rows."""
+    int32; context_lens [B] int32; tree_mask [B, R, W] int64 bit rows.  timeout_ns bounds
+    every wait of the kernel (0 = the library default, 2 s); a wait that runs out
+    records CF_ETIMEOUT in `status` and the output is then undefined."""
     B = context_lens.shape[0]
     if out is None:
         out = torch.empty_like(q)
@@ -58,7 +60,7 @@ def verify_attention(cache, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_
                         max_context=int(max_context), tree_mask=_ptr(tree_mask),
                         mask_words=tree_mask.shape[-1] if tree_mask is not None else 0,
                         out=out.data_ptr(), out_row_stride=out.stride(0), scale=0.0, num_splits=num_splits,
-                        status=_ptr(status), trace=_ptr(trace))
+                        status=_ptr(status), timeout_ns=timeout_ns, trace=_ptr(trace))
     L = _lib.lib()
     need = L.cf_attention_workspace_bytes(ctypes.byref(a))
     if need:

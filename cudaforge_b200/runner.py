@@ -31,7 +31,9 @@ class PagedRunner:
         self.committed = [0] * len(self.seq_ids)
         self.registered = False
         self.last = None  # (start[b], R) of the last forward
-        self.status = torch.zeros(1, dtype=torch.int32, device=model.device)
+        from . import _lib
+        self.st = _lib.DeviceStatus(model.device)
+        self.status = self.st.dev
 
     @property
     def device(self):

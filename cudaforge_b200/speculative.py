@@ -137,6 +137,10 @@ class SpeculativeEngine:
                 runner.commit_upto(upto)
         torch.cuda.synchronize(dev)
         t2 = time.perf_counter()
+        for runner in (self.target_runner, self.draft_runner):
+            st = getattr(runner, "st", None)
+            if st is not None:  # a bounded wait that ran out or a bad page id voids the step
+                st.sync_check(type(runner).__name__)
         B, K = draft_tokens.shape
         width = max(n_host)
         tok = res.tokens.cpu()

@@ -238,7 +238,9 @@ class TreeVerifier:
         res = accept_tree(None if b.greedy else draft_logits, logits.view(B, N1, -1), self.parent, b.tokens, uniforms,
                           temperature=b.temperature, eos_token_id=b.eos, greedy=b.greedy, workspace=self.ws)
         b.n_pinned.copy_(res.num_accepted, non_blocking=True)
+        b.st.snapshot()
         torch.cuda.current_stream(b.model.device).synchronize()
+        b.st.check("TreeVerifier.step")
         n = [max(0, int(x)) + 1 for x in b.n_pinned.tolist()]
         start = b.ctx.clone()
         b.cache.append_batch(b.seq_ids, n)
@@ -252,3 +254,6 @@ class TreeVerifier:
         idx = res.num_accepted.clamp_min(0).long().view(B, 1)
         b.tokens[:, :1].copy_(res.tokens.gather(1, idx))
         return res
+
+    def check_status(self) -> None:
+        self.base.check_status()

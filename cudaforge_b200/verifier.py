@@ -57,7 +57,9 @@ class BatchVerifier:
                                 num_accepted=torch.zeros(B, dtype=torch.int32, device=dev),
                                 eos=torch.zeros(B, dtype=torch.bool, device=dev))
         self.ws = torch.empty(4096 + 16 * B * (2 * k + 1), dtype=torch.uint8, device=dev)
-        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        from . import _lib
+        self.st = _lib.DeviceStatus(dev)  # every kernel of the step records CF_ETIMEOUT / CF_ERANGE here
+        self.status = self.st.dev
         self.model.buffers(B, R)
         # CUDA graphs (single-GPU models only: the TP collectives stay eager)
         self.use_graph = use_graph and getattr(model, "tp", None) is None
@@ -109,16 +111,20 @@ class BatchVerifier:
         logits = self.model.forward_rows(self.cache, self.tokens, self.pos, self.tables(), self.ctx,
                                          max_context if max_context is not None else max(self.ctx_host),
                                          status=self.status, timer=timer)
-        return accept_sample(draft_logits, logits.view(B, R, -1), draft_tokens, uniforms,
-                             temperature=self.temperature, eos_token_id=self.eos, greedy=self.greedy,
-                             workspace=self.ws, out=self.res)
+        from .model import _null_timer
+        with (timer or _null_timer)("accept"):
+            return accept_sample(draft_logits, logits.view(B, R, -1), draft_tokens, uniforms,
+                                 temperature=self.temperature, eos_token_id=self.eos, greedy=self.greedy,
+                                 workspace=self.ws, out=self.res)
 
-    def _commit_update(self, res: AcceptResult) -> None:
+    def _commit_update(self, res: AcceptResult, timer=None) -> None:
+        from .model import _null_timer
         B, R = self.B, self.R
         bf = self.model.buffers(B, R)
         self.start.copy_(self.ctx)
-        ops.kv_commit(self.cache, bf["k_new"], bf["v_new"], res.num_accepted, self.start, self.tables(),
-                      n_commit_add=1, status=self.status)
+        with (timer or _null_timer)("commit"):
+            ops.kv_commit(self.cache, bf["k_new"], bf["v_new"], res.num_accepted, self.start, self.tables(),
+                          n_commit_add=1, status=self.status)
         # next round: context grows by n, row 0 = the final token
         self.ctx.add_(res.num_accepted.clamp_min(0) + 1)
         idx = res.num_accepted.clamp_min(0).long().view(B, 1)
@@ -126,8 +132,6 @@ class BatchVerifier:
 
     def _capture(self, draft_tokens, draft_logits, uniforms) -> None:
         from . import gemm as _gemm
-        # hold every workspace the captured kernels address (the caches may grow later)
-        self._keep = [dict(ops._Ws.bufs), dict(_gemm._Ws.bufs)]
         g_tok = draft_tokens.to(dtype=torch.int32).clone()
         g_uni = None if uniforms is None else uniforms.clone()
         self.g_in = (g_tok, draft_logits, g_uni)  # draft logits are captured by address
@@ -138,6 +142,10 @@ class BatchVerifier:
         with torch.cuda.graph(g2):
             self._commit_update(self.res)
         self.graphs = (g1, g2)
+        # hold every workspace the captured kernels address: the capture plans for
+        # max_context, which can grow a cached workspace inside the capture, and a
+        # later call may replace the cache entry while this graph still uses it
+        self._keep = [dict(ops._Ws.bufs), dict(_gemm._Ws.bufs)]
 
     @torch.no_grad()
     def step(self, draft_tokens: torch.Tensor, draft_logits: Optional[torch.Tensor],
@@ -165,7 +173,10 @@ class BatchVerifier:
         else:
             res = self._forward_accept(draft_tokens, draft_logits, uniforms, timer=timer)
         self.n_pinned.copy_(res.num_accepted, non_blocking=True)
+        self.st.snapshot()
         torch.cuda.current_stream(self.model.device).synchronize()
+        # a bounded wait that ran out or a bad page id makes the step's results meaningless
+        self.st.check("BatchVerifier.step")
         n = [max(0, int(x)) + 1 for x in self.n_pinned.tolist()]
         self.cache.append_batch(self.seq_ids, n)
         self._upload_tables()
@@ -173,8 +184,13 @@ class BatchVerifier:
             self.graphs[1].replay()
             _lib.count(self.kernels_per_step)
         else:
-            self._commit_update(res)
+            self._commit_update(res, timer=timer)
             if not self.kernels_per_step:
                 self.kernels_per_step = _lib.LAUNCHES[0] - l0
         self.ctx_host = [c + x for c, x in zip(self.ctx_host, n)]
         return res
+
+    def check_status(self) -> None:
+        """Synchronise and raise DeviceError if a kernel since the last check
+        (e.g. the last step's KV commit) recorded an error."""
+        self.st.sync_check("BatchVerifier")

@@ -121,7 +121,10 @@ int cf_accept_sample(const cf_accept_args *args, void *stream);
  * library, held until exit).  batch * (2k + 1) beyond that limit returns
  * CF_ERANGE and launches nothing.  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture.  All calls share the array: calls that can run
+ * before any stream capture.  The address is cached per device ordinal for
+ * the life of the process: after cudaDeviceReset (or any teardown of the
+ * device's primary context) it is stale, so do not call this entry point
+ * again in that process.  All calls share the array: calls that can run
  * at the same time on the GPU (different streams, different host threads)
  * race and must be serialised by the caller.  No cudaMalloc / cudaFree. */
 int cf_accept_sample_noalloc(const cf_accept_args *args, void *stream);

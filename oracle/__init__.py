@@ -18,8 +18,15 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 _P = ctypes.c_void_p
 
 
-def build() -> None:
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+def build(reference_root=None) -> None:
+    """Build liboracle.so and, when a reference checkout is given (argument or
+    the CF_REFERENCE_ROOT environment variable), the compiled-reference
+    checkers under oracle/_ref."""
+    ref = reference_root or os.environ.get("CF_REFERENCE_ROOT", "")
+    cmd = ["make", "-s", "-C", HERE]
+    if ref and os.path.isdir(ref):
+        cmd.append(f"REF={ref}")
+    subprocess.run(cmd, check=True)
 
 
 def _load(path):

@@ -109,3 +109,42 @@ def forward_full(model, tokens, tree_parent=None):
         x = x + act @ linear_weight_fp32(lay["down"]).T
     x = rmsnorm(x, model.final_norm, c.eps)
     return x @ linear_weight_fp32(model.lm_head).T
+
+
+def forward_rows(model, key_pool, value_pool, tables, ctx_lens, tokens, tree_mask=None, depth=None, bs=16):
+    """fp32 restatement of the incremental verify forward (LlamaModel.forward_rows):
+    the R new rows tokens [B, R] of every sequence at positions ctx_lens[b] + r
+    (or ctx_lens[b] + depth[r] for a tree) attend to the cached context read
+    from the paged pools ([blocks, L, Hkv, bs, D], the kernels' own inputs, so
+    any cache contents serve) and to the new rows under a causal or tree mask
+    (tree_mask [B, R, R] bool).  Weights are dequantised exactly.  Returns
+    logits [B, R, V] fp32."""
+    from cudaforge_b200.model import linear_weight_fp32
+
+    c = model.cfg
+    B, R = tokens.shape
+    dev = model.embed.device
+    tokens = tokens.to(dev).long()
+    ctx = torch.as_tensor(ctx_lens).to(dev).long()
+    off = torch.arange(R, device=dev) if depth is None else torch.as_tensor(depth, device=dev).long()
+    pos = ctx.view(B, 1) + off.view(1, R)  # [B, R]
+    x = model.embed.float()[tokens]  # [B, R, d]
+    tables_cpu = torch.as_tensor(tables).cpu()
+    ctx_cpu = ctx.cpu()
+    for li, lay in enumerate(model.layers):
+        xn = rmsnorm(x, lay["attn_norm"], c.eps)
+        qkv = xn @ linear_weight_fp32(lay["qkv"]).T
+        q = qkv[..., : c.n_heads * c.head_dim].view(B, R, c.n_heads, c.head_dim)
+        k = qkv[..., c.n_heads * c.head_dim:(c.n_heads + c.n_kv_heads) * c.head_dim].view(B, R, c.n_kv_heads,
+                                                                                           c.head_dim)
+        v = qkv[..., (c.n_heads + c.n_kv_heads) * c.head_dim:].view(B, R, c.n_kv_heads, c.head_dim)
+        q = rope(q, pos.view(B, R, 1), c.rope_base)
+        k = rope(k, pos.view(B, R, 1), c.rope_base)
+        a = verify_attention(q, key_pool, value_pool, li, tables_cpu, ctx_cpu, k, v, tree_mask=tree_mask, bs=bs)
+        x = x + a.reshape(B, R, -1) @ linear_weight_fp32(lay["o"]).T
+        xn = rmsnorm(x, lay["ffn_norm"], c.eps)
+        gu = xn @ linear_weight_fp32(lay["gate_up"]).T
+        act = torch.nn.functional.silu(gu[..., : c.ffn]) * gu[..., c.ffn:]
+        x = x + act @ linear_weight_fp32(lay["down"]).T
+    x = rmsnorm(x, model.final_norm, c.eps)
+    return x @ linear_weight_fp32(model.lm_head).T

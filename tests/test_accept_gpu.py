@@ -141,3 +141,33 @@ def test_shape_errors_raise_value_error():
         accept_sample(d[:, :2], d, torch.zeros(2, 3, dtype=torch.int32).cuda(), torch.rand(2, 4).cuda())
     with pytest.raises(ValueError):
         accept_sample(d[:, :3], d, torch.zeros(2, 3, dtype=torch.int32).cuda(), None)
+
+
+@pytest.mark.parametrize("mode", ["close", "far", "same", "mixed"])
+def test_cfg3_shape_parity(mode):
+    """The benchmark's acceptance shape: B=64, K=5, V=128,256 bf16 logits (32
+    scan chunks of 4,096 per row), stochastic and greedy."""
+    B, K, V = 64, 5, 128256
+    g = torch.Generator(device="cuda").manual_seed({"close": 1, "far": 2, "same": 3, "mixed": 4}[mode])
+    d = torch.randn(B, K + 1, V, generator=g, device="cuda") * 2.0
+    if mode == "close":
+        t = d + 0.3 * torch.randn(B, K + 1, V, generator=g, device="cuda")
+    elif mode == "far":
+        t = torch.randn(B, K + 1, V, generator=g, device="cuda") * 3.0
+    elif mode == "same":
+        t = d.clone()
+    else:  # per sequence a different closeness: rejections at every position
+        w = torch.linspace(0.0, 2.0, B, device="cuda").view(B, 1, 1)
+        t = d + w * torch.randn(B, K + 1, V, generator=g, device="cuda")
+    d, t = d.to(torch.bfloat16), t.to(torch.bfloat16)
+    dtoks = torch.multinomial(torch.softmax(d[:, :K].float().reshape(-1, V), -1), 1, generator=g).reshape(B, K)
+    u = torch.rand(B, K + 1, generator=g, device="cuda")
+    res = accept_sample(d[:, :K], t, dtoks, u, export_probs=True)
+    torch.cuda.synchronize()
+    na = _check_parity(res, dtoks, u, -1)
+    if mode == "mixed":
+        assert len(set(na.tolist())) >= 3  # several rejection positions exercised
+    if mode == "far":
+        res = accept_sample(None, t, dtoks, greedy=True, export_probs=True)
+        torch.cuda.synchronize()
+        _check_parity(res, dtoks, None, -1, greedy=True)

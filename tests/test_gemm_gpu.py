@@ -3,9 +3,11 @@
 Two checks per case: (1) against the exact fp32 dequantisation
 w = (nibble - 8) * scale (the reference test's semantics,
 tests/unit/test_int4_dequant.py:18-53) with the max error relative to the
-largest output <= 1e-2; (2) against an fp32 GEMM over the bf16 weights the
-kernel actually multiplies, max relative error <= 5e-3 (bf16 output rounding) (catches any indexing
-error, which the looser bound might hide)."""
+largest output <= 1e-2; (2) against an fp32 GEMM over the weights rounded as the reference rounds
+them (fp32 dequantisation cast once to bf16, int4_dequant_triton.py:66),
+max relative error <= 5e-3 (bf16 output rounding; catches any indexing error
+the looser bound might hide); (3) the kernel's dequantised weights equal
+those reference-rounded weights bit for bit (identity activations)."""
 import pytest
 import torch
 
@@ -39,11 +41,32 @@ def test_w4a16_vs_fp32(M, N, K, split):
     y = w4a16_gemm(x.cuda(), wk, s.cuda(), split_k=split)
     torch.cuda.synchronize()
     assert _rel(y.cpu(), ref) < 1e-2
-    # emulate the kernel's weight rounding: bf16((q - 8) * bf16(scale))
-    sb = s.float().to(torch.bfloat16).float().repeat_interleave(128, 0)
-    w_bf = ((q.float() - 8.0) * sb).to(torch.bfloat16).float()
+    # the reference's weight rounding (int4_dequant_triton.py:66): the exact fp32 product
+    # (q - 8) * scale cast once to the activation type
+    w_bf = dequant_reference(wq, s).to(torch.bfloat16).float()
     ref2 = x.float() @ w_bf
     assert _rel(y.cpu(), ref2) < 5e-3  # bf16 output rounding is 2^-9 relative
+
+
+def test_w4a16_weight_rounding_matches_reference():
+    """x = identity rows picks single weight rows out of the GEMM: y[m, n] is then
+    exactly the kernel's dequantised w[k=m, n] (one non-zero product, fp32
+    accumulation, bf16 output of a bf16 value), which must equal the reference's
+    bf16((q - 8) * float(scale)) bit for bit -- scales cover normal and subnormal
+    fp16 values."""
+    K, N = 256, 256
+    g = torch.Generator().manual_seed(11)
+    q = torch.randint(0, 16, (K, N), generator=g)
+    s = (torch.randn(K // 128, N, generator=g).abs() * 0.002)
+    s[:, :32] = torch.rand(K // 128, 32, generator=g) * 6e-5   # subnormal fp16 scales
+    s[:, 32:64] = torch.rand(K // 128, 32, generator=g) * 8.0  # large scales
+    s = s.to(torch.float16)
+    wq = pack_int4_reference(q)
+    x = torch.eye(K, dtype=torch.bfloat16)
+    y = w4a16_gemm(x.cuda(), repack_int4(wq.cuda()), s.cuda())
+    torch.cuda.synchronize()
+    ref = dequant_reference(wq, s).to(torch.bfloat16)
+    assert torch.equal(y.cpu(), ref)
 
 
 def test_w4a16_residual_and_strided_out():

@@ -48,3 +48,54 @@ def test_graph_step_matches_eager():
     assert vs[1].graphs is not None
     for pa, pb in ((vs[0].cache.key_pool, vs[1].cache.key_pool), (vs[0].cache.value_pool, vs[1].cache.value_pool)):
         assert torch.equal(pa, pb)
+
+
+def test_graph_workspaces_outlive_later_captures():
+    """Each captured graph holds every cached workspace it addresses: after the
+    verifier captures, and then a drafter captures (and may grow the shared
+    workspace caches), the verifier's graph still replays correctly and every
+    buffer present in the caches right after each capture is held by that
+    graph's owner."""
+    from cudaforge_b200 import gemm as _gemm
+    from cudaforge_b200 import ops
+    from cudaforge_b200.drafter import BatchDrafter
+
+    cfg = LlamaConfig(2, 512, 8, 2, 128, 768, 2048)
+    m = LlamaModel(cfg, seed=8)
+    B, K, P = 5, 4, 200
+    g = torch.Generator().manual_seed(1)
+    prompts = torch.randint(0, cfg.vocab, (B, P), generator=g)
+    cache = m.make_cache(B * 40, max_batch=B)
+    v = BatchVerifier(m, cache, list(range(B)), K, max_blocks_per_seq=30, use_graph=True)
+    v.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
+    v.fill_synthetic_kv(torch.Generator(device="cuda").manual_seed(2))
+    gd = torch.Generator(device="cuda").manual_seed(3)
+    dlog = torch.randn(B, K, cfg.vocab, generator=gd, device="cuda").to(cfg.dtype)
+    dtok = torch.randint(0, cfg.vocab, (B, K), generator=gd, device="cuda", dtype=torch.int32)
+    u = torch.rand(B, K + 1, generator=gd, device="cuda")
+    v.step(dtok, dlog, u)
+    v.step(dtok, dlog, u)  # capture + replay
+    assert v.graphs is not None
+
+    def held(keep):
+        ids = {id(b) for d in keep for b in d.values()}
+        return all(id(b) in ids for b in list(ops._Ws.bufs.values()) + list(_gemm._Ws.bufs.values()))
+
+    assert held(v._keep)
+    dcache = m.make_cache(B * 40, max_batch=B)
+    dr = BatchDrafter(m, dcache, list(range(B)), K, max_blocks_per_seq=30, use_graph=True)
+    dr.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
+    dr.draft(u[:, :K].contiguous())
+    dr.draft(u[:, :K].contiguous())  # the drafter captures its graph
+    assert dr.graph is not None and held(dr._keep)
+    # the verifier's graph replays after the drafter's capture, still bit-identical to eager
+    ve = BatchVerifier(m, m.make_cache(B * 40, max_batch=B), list(range(B)), K, max_blocks_per_seq=30)
+    ve.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
+    ve.fill_synthetic_kv(torch.Generator(device="cuda").manual_seed(2))
+    ve.step(dtok, dlog, u)
+    ve.step(dtok, dlog, u)
+    a = v.step(dtok, dlog, u)
+    b = ve.step(dtok, dlog, u)
+    torch.cuda.synchronize()
+    assert torch.equal(a.num_accepted, b.num_accepted) and torch.equal(a.tokens, b.tokens)
+    v.check_status()

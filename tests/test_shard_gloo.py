@@ -7,7 +7,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from cudaforge_b200.shard import rank_sequence_ids, reduce_step_metrics
+from cudaforge_b200.shard import gather_emitted, rank_sequence_ids, reduce_step_metrics, split_global_batch
 
 
 def _worker(rank, world, port, q):
@@ -16,7 +16,11 @@ def _worker(rank, world, port, q):
     try:
         ids = rank_sequence_ids(rank, 4)
         times, toks = reduce_step_metrics([10.0 + rank, 20.0 - rank], [100.0 * (rank + 1), 7.0])
-        q.put((rank, ids, times, toks))
+        # strong scaling: a global batch of 8 split over the ranks, emitted tokens gathered on rank 0
+        b = split_global_batch(8, world)
+        gids = rank_sequence_ids(rank, b)
+        got = gather_emitted(gids, [[g, g + 100] for g in gids])
+        q.put((rank, ids, times, toks, got))
     finally:
         dist.destroy_process_group()
 
@@ -36,11 +40,21 @@ def test_two_rank_reduction_and_disjoint_shards():
         assert p.exitcode == 0
     out.sort()
     assert out[0][1] == [0, 1, 2, 3] and out[1][1] == [4, 5, 6, 7]
-    for _, _, times, toks in out:
+    for _, _, times, toks, _ in out:
         assert times == [11.0, 20.0]   # max over ranks
         assert toks == [300.0, 14.0]   # sum over ranks
+    assert out[0][4] == {g: [g, g + 100] for g in range(8)}  # rank 0 holds every sequence
+    assert out[1][4] is None
 
 
 def test_single_process_is_identity():
     times, toks = reduce_step_metrics([1.5], [3.0])
     assert times == [1.5] and toks == [3.0]
+    assert gather_emitted([3, 4], [[1], [2, 5]]) == {3: [1], 4: [2, 5]}
+
+
+def test_split_global_batch():
+    assert [split_global_batch(64, n) for n in (1, 2, 4, 8)] == [64, 32, 16, 8]
+    import pytest
+    with pytest.raises(ValueError):
+        split_global_batch(64, 3)
