@@ -342,7 +342,7 @@ def run_ours(args):
 
     # ---- full speculative rounds: draft loop (K steps of the 1B draft) + verify + accept + advance ----
     round_info = None
-    if drafter is not None:
+    if drafter is not None and not args.no_rounds:
         ud = torch.rand(args.steps + 2, B, K, generator=gen, device=device)
         for i in range(2):  # the drafter captures its graph on its second round
             dt_, dl_ = drafter.draft(ud[i])
@@ -707,6 +707,7 @@ def main():
     ap.add_argument("--temperature", type=float, default=1.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every kernel eagerly (no CUDA graphs)")
+    ap.add_argument("--no-rounds", action="store_true", help="skip the full-round (draft loop) timing")
     ap.add_argument("--case", default=None, choices=["gemm", "attention", "accept"],
                     help="time a single kernel at the bench shapes (profiling aid)")
     ap.add_argument("--shape", default=None, help="NxK for --case gemm")

@@ -87,7 +87,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
   uint32_t n = 0;
   while (true) {
     if (mbar_test_wait(bar, parity)) return true;
-    if ((++n & 255u) == 0 && globaltimer() - t0 > limit_ns) return false;
+    // the clock is read every 16 polls (a fraction of a microsecond), so even a
+    // limit far below the pipeline's own latencies is observed reliably
+    if ((++n & 15u) == 0 && globaltimer() - t0 > limit_ns) return false;
   }
 }
 

@@ -36,6 +36,7 @@
 #include "tmap.h"
 
 #include <algorithm>
+#include <mutex>
 #include <cstdlib>
 
 namespace {
@@ -528,7 +529,23 @@ int run_gemm(const cf_gemm_args &a, cudaStream_t stream, bool partials_only = fa
   p.timeout_ns = a.timeout_ns ? a.timeout_ns : 2000000000ull;
   p.trace = reinterpret_cast<unsigned long long *>(a.trace);
   auto kern = gemm_kernel<T, WM>;
-  CF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+  // The dynamic shared memory of a launch depends on the plan (token slice), but the
+  // function attribute is per kernel function: raise it once per device to the largest
+  // plan and never lower it, or a CUDA graph captured with a larger plan would fail to
+  // replay after a smaller plan's launch had lowered the limit.
+  {
+    static std::mutex mu;
+    static bool raised[64][2][2];
+    int dev = 0;
+    CF_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> g(mu);
+    bool &done = raised[dev & 63][std::is_same<T, __half>::value][WM];
+    if (!done) {
+      CF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+      done = true;
+    }
+  }
+  if (pl.smem > (size_t)kMaxSmem) return CF_EINVAL;
   dim3 grid(pl.slices, pl.ntiles, pl.splits);
   kern<<<grid, kThreads, pl.smem, stream>>>(tx, tw, ts, p);
   if (cudaGetLastError() != cudaSuccess) return CF_ECUDA;

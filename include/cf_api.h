@@ -445,6 +445,44 @@ int cf_splitk_rope_qkv(const float *partials, int32_t splits, int32_t m, void *q
 int cf_splitk_silu_mul(const float *partials, int32_t splits, int32_t m, int32_t ffn, void *out, int64_t ldo,
                        int32_t dtype, void *stream);
 
+/* ---------------------------------------------------------------------------
+ * Host speculative verification engine.  Replaces the reference's native
+ * SpeculativeEngine (csrc/include/cudaforge/scheduler/speculative.h:14-85,
+ * csrc/src/scheduler/speculative.cpp:8-150, bound at
+ * csrc/bindings/pybind_module.cpp:199-239): a configuration plus a
+ * std::mt19937 stream seeded with rng_seed, drawn with
+ * std::uniform_real_distribution<float>(0, 1) in the reference's order, so a
+ * sequence of calls gives the reference engine's outputs.  Per-sequence
+ * probability rows (host memory, possibly ragged: row i has lens[i] floats).
+ * cf_spec_engine_verify: stochastic (greedy = 0; n_draft must equal k,
+ * speculative.cpp:58-62) or greedy (greedy = 1; draft rows unused,
+ * speculative.cpp:105-150); n_target >= k + 1 (CF_EINVAL otherwise).
+ * out_accepted[0..num_accepted) are the accepted drafts, out_final_token the
+ * correction / bonus / EOS token.  A draft token outside its rows returns
+ * CF_ERANGE (the reference reads out of bounds).  Calls on one engine are
+ * serialised by its mutex.  cf_spec_engine_draw_uniforms: the next n values
+ * of the engine's stream (for cf_accept_sample's uniforms).
+ * ------------------------------------------------------------------------- */
+typedef struct cf_spec_config {
+  int64_t gamma;       /* draft tokens per step (K); stored, as in the reference */
+  float temperature;   /* stored; the probability rows are already softmaxed */
+  float top_p;         /* stored; unused by verification (speculative.h:17) */
+  uint64_t rng_seed;   /* seeds the engine's stream once, at creation */
+} cf_spec_config;
+
+typedef struct cf_spec_engine cf_spec_engine;
+
+int cf_spec_engine_create(const cf_spec_config *config, cf_spec_engine **out);
+void cf_spec_engine_destroy(cf_spec_engine *engine);
+int cf_spec_engine_set_config(cf_spec_engine *engine, const cf_spec_config *config);
+int cf_spec_engine_get_config(cf_spec_engine *engine, cf_spec_config *out);
+int cf_spec_engine_verify(cf_spec_engine *engine, int32_t k, const int32_t *draft_tokens,
+                          const float *const *draft_rows, const int64_t *draft_lens, int32_t n_draft,
+                          const float *const *target_rows, const int64_t *target_lens, int32_t n_target,
+                          int32_t eos_token_id, int32_t greedy, int32_t *out_accepted,
+                          int32_t *out_num_accepted, int32_t *out_final_token, int32_t *out_eos);
+int cf_spec_engine_draw_uniforms(cf_spec_engine *engine, int64_t n, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -159,6 +159,26 @@ def ref_verify(seed, draft_tokens, draft_probs, target_probs, eos):
     return tok, int(na[0]), int(ef[0])
 
 
+def ref_verify_stream(seed, draft_tokens, draft_probs, target_probs, eos):
+    """B consecutive verify_candidates calls on one reference engine seeded
+    with `seed` (its random stream carries over).  draft_tokens [B,K],
+    draft_probs [B,K,V], target_probs [B,K+1,V].  Returns (tokens [B,K+1],
+    num_accepted [B], eos [B])."""
+    dt = np.ascontiguousarray(draft_tokens, dtype=np.int32)
+    dp = np.ascontiguousarray(draft_probs, dtype=np.float32)
+    tp = np.ascontiguousarray(target_probs, dtype=np.float32)
+    B, K = dt.shape
+    V = tp.shape[-1]
+    tok = np.full((B, K + 1), -1, np.int32)
+    na = np.zeros(B, np.int32)
+    ef = np.zeros(B, np.uint8)
+    rc = ref().ref_verify_stream(ctypes.c_uint64(seed), ctypes.c_int32(B), ctypes.c_int32(K), ctypes.c_int64(V),
+                                 _ptr(dt), _ptr(dp), _ptr(tp), ctypes.c_int32(eos), _ptr(tok), _ptr(na), _ptr(ef))
+    if rc != 0:
+        raise ValueError("reference verify_candidates raised")
+    return tok, na, ef
+
+
 def ref_verify_greedy(draft_tokens, target_probs, eos):
     dt = np.ascontiguousarray(draft_tokens, dtype=np.int32)
     tp = np.ascontiguousarray(target_probs, dtype=np.float32)
@@ -242,3 +262,69 @@ class RefKV:
         out = np.zeros(8, np.uint64)
         self.lib().refkv_stats(self.h, _ptr(out))
         return out.tolist()
+
+
+class RefSched:
+    """ctypes front end to oracle/_ref/libsched_ref.so (the reference
+    ContinuousBatcher + ModelRunner)."""
+
+    _L = None
+
+    @classmethod
+    def available(cls) -> bool:
+        return os.path.exists(os.path.join(HERE, "_ref", "libsched_ref.so"))
+
+    @classmethod
+    def _lib(cls):
+        if cls._L is None:
+            L = ctypes.CDLL(os.path.join(HERE, "_ref", "libsched_ref.so"))
+            L.rs_create.restype = ctypes.c_void_p
+            L.rs_create.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int32]
+            L.rs_destroy.argtypes = [ctypes.c_void_p]
+            L.rs_add.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                 ctypes.c_int32]
+            L.rs_cancel.argtypes = [ctypes.c_void_p, ctypes.c_uint64]
+            L.rs_update.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32]
+            L.rs_step.restype = ctypes.c_uint64
+            L.rs_step.argtypes = [ctypes.c_void_p]
+            L.rs_pop.restype = ctypes.c_int32
+            L.rs_pop.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32]
+            L.rs_pending.restype = ctypes.c_uint64
+            L.rs_pending.argtypes = [ctypes.c_void_p]
+            L.rs_running.restype = ctypes.c_uint64
+            L.rs_running.argtypes = [ctypes.c_void_p]
+            cls._L = L
+        return cls._L
+
+    def __init__(self, max_seqs, max_tokens, vocab, eos):
+        self.h = self._lib().rs_create(max_seqs, max_tokens, vocab, eos)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self._lib().rs_destroy(self.h)
+            self.h = None
+
+    def add(self, rid, prompt, max_tokens, priority):
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        return bool(self._lib().rs_add(self.h, rid, _ptr(p) if p.size else None, p.size, max_tokens, priority))
+
+    def cancel(self, rid):
+        self._lib().rs_cancel(self.h, rid)
+
+    def update(self, ids):
+        a = np.ascontiguousarray(ids, dtype=np.uint64)
+        self._lib().rs_update(self.h, _ptr(a) if a.size else None, a.size)
+
+    def step(self):
+        return int(self._lib().rs_step(self.h))
+
+    def pop(self):
+        cap = 4096
+        ids = np.zeros(cap, np.uint64)
+        tok = np.zeros(cap, np.int32)
+        fin = np.zeros(cap, np.uint8)
+        n = self._lib().rs_pop(self.h, _ptr(ids), _ptr(tok), _ptr(fin), cap)
+        return [(int(ids[i]), int(tok[i]), bool(fin[i])) for i in range(min(n, cap))]
+
+    def counts(self):
+        return int(self._lib().rs_pending(self.h)), int(self._lib().rs_running(self.h))

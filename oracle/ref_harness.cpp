@@ -89,4 +89,35 @@ int ref_verify_batch(uint64_t seed, int32_t B, int32_t K, int64_t V,
   }
   return 0;
 }
+
+// B consecutive verify_candidates calls on ONE engine seeded with `seed`
+// (the engine's stream carries over between calls, speculative.h:70-82);
+// sequence b is call b.
+int ref_verify_stream(uint64_t seed, int32_t B, int32_t K, int64_t V,
+                      const int32_t *draft_tokens, const float *draft_probs,
+                      const float *target_probs, int32_t eos, int32_t *tokens,
+                      int32_t *num_accepted, uint8_t *eos_flag) {
+  SpeculativeConfig cfg;
+  cfg.gamma = (size_t)K;
+  cfg.rng_seed = seed;
+  SpeculativeEngine eng(cfg);
+  for (int b = 0; b < B; ++b) {
+    std::vector<int32_t> dt(draft_tokens + (size_t)b * K, draft_tokens + (size_t)(b + 1) * K);
+    std::vector<std::vector<float>> dp(K), tp(K + 1);
+    const float *d = draft_probs + (size_t)b * K * V, *t = target_probs + (size_t)b * (K + 1) * V;
+    for (int i = 0; i < K; ++i) dp[i].assign(d + (size_t)i * V, d + (size_t)(i + 1) * V);
+    for (int i = 0; i <= K; ++i) tp[i].assign(t + (size_t)i * V, t + (size_t)(i + 1) * V);
+    try {
+      auto r = eng.verify_candidates(dt, dp, tp, eos);
+      int32_t *o = tokens + (size_t)b * (K + 1);
+      for (size_t i = 0; i < r.accepted_tokens.size(); ++i) o[i] = r.accepted_tokens[i];
+      o[r.num_accepted] = r.final_token;
+      num_accepted[b] = (int32_t)r.num_accepted;
+      eos_flag[b] = r.end_of_sequence ? 1 : 0;
+    } catch (...) {
+      return -1;
+    }
+  }
+  return 0;
+}
 }

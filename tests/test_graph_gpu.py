@@ -99,3 +99,27 @@ def test_graph_workspaces_outlive_later_captures():
     torch.cuda.synchronize()
     assert torch.equal(a.num_accepted, b.num_accepted) and torch.equal(a.tokens, b.tokens)
     v.check_status()
+
+
+def test_gemm_graph_replays_after_smaller_plan():
+    """A captured GEMM (large token slice, large dynamic shared memory) must
+    still replay after an eager GEMM with a smaller plan ran on the same
+    kernel function (the per-function shared-memory limit is never lowered)."""
+    from cudaforge_b200.gemm import w4a16_gemm
+    g = torch.Generator(device="cuda").manual_seed(4)
+    N, K = 1024, 1024
+    wq = torch.randint(-2**31, 2**31 - 1, (K // 8, N), generator=g, device="cuda", dtype=torch.int32)
+    sc = (torch.rand(K // 128, N, generator=g, device="cuda") * 0.002).half()
+    xb = torch.randn(384, K, generator=g, device="cuda").to(torch.bfloat16)
+    xs = torch.randn(16, K, generator=g, device="cuda").to(torch.bfloat16)
+    yb = torch.empty(384, N, dtype=torch.bfloat16, device="cuda")
+    w4a16_gemm(xb, wq, sc, out=yb)
+    ref = yb.clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        w4a16_gemm(xb, wq, sc, out=yb)
+    yb.zero_()
+    w4a16_gemm(xs, wq, sc)  # smaller plan, same kernel function
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(yb, ref)
