@@ -56,32 +56,77 @@ __global__ void rmsnorm_kernel(const T *x, int64_t ldx, const T *w, T *out, int6
   }
 }
 
-// One CTA per row m; threads over (head, i < D/2) pairs for the Hq + Hkv
-// rotated heads, then the V copy.
+// RoPE (half split): the row's rotation table, (cos, sin) of p * base^(-2i/D)
+// for i < D/2, computed once per row in shared memory (every head of the row
+// shares it), with explicitly rounded products (no FMA contraction) so the
+// plain and the split-K kernels below compute the same bits.
+constexpr int kMaxHalf = 128;  // head_dim <= 256
+
+__device__ __forceinline__ void rope_table(float p, int D, float log2_base, float2 *tab) {
+  for (int i = threadIdx.x; i < D / 2; i += blockDim.x) {
+    const float inv_freq = exp2f(__fmul_rn(-__fdiv_rn((float)(2 * i), (float)D), log2_base));
+    float sn, cs;
+    sincosf(__fmul_rn(p, inv_freq), &sn, &cs);
+    tab[i] = make_float2(cs, sn);
+  }
+  __syncthreads();
+}
+
+// Four consecutive pairs (x1[j], x2[j]) = (x[i0+j], x[i0+j+D/2]).
+__device__ __forceinline__ void rope4(const float2 *tab, int i0, const float (&x1)[4], const float (&x2)[4],
+                                      float (&o1)[4], float (&o2)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = tab[i0 + j];
+    o1[j] = __fsub_rn(__fmul_rn(x1[j], t.x), __fmul_rn(x2[j], t.y));
+    o2[j] = __fadd_rn(__fmul_rn(x1[j], t.y), __fmul_rn(x2[j], t.x));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void load4(const T *p, float (&o)[4]) {
+  const uint2 r = *reinterpret_cast<const uint2 *>(p);
+  const T *t = reinterpret_cast<const T *>(&r);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[j] = cf::to_float(t[j]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store4(T *p, const float (&v)[4]) {
+  uint2 r;
+  T *t = reinterpret_cast<T *>(&r);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) t[j] = from_f<T>(v[j]);
+  *reinterpret_cast<uint2 *>(p) = r;
+}
+
+// Where the rotated pairs of head hh go: q heads back into the qkv row, k heads
+// into this step's K scratch [m][Hkv][D].
+template <typename T>
+__device__ __forceinline__ T *rope_dst(T *row, T *k_new, int m, int hh, int Hq, int Hkv, int D) {
+  return hh < Hq ? row + (int64_t)hh * D : k_new + ((int64_t)m * Hkv + (hh - Hq)) * D;
+}
+
+// One CTA per row m.  Work items: (head, 4 pairs) for the Hq + Hkv rotated
+// heads (8-byte vector accesses), then 16-byte copies of the V heads.
 template <typename T>
 __global__ void rope_qkv_kernel(T *qkv, int64_t ld, int Hq, int Hkv, int D, const int32_t *pos, float log2_base,
                                 T *k_new, T *v_new) {
   const int m = blockIdx.x;
   T *row = qkv + (int64_t)m * ld;
-  const float p = (float)pos[m];
-  const int half = D / 2;
-  const int pairs = (Hq + Hkv) * half;
-  for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
-    const int hh = idx / half, i = idx % half;
-    const float inv_freq = exp2f(-((float)(2 * i) / (float)D) * log2_base);
-    float s, c;
-    sincosf(p * inv_freq, &s, &c);
-    const T *src = row + (int64_t)hh * D;
-    const float x1 = cf::to_float(src[i]), x2 = cf::to_float(src[i + half]);
-    const float o1 = x1 * c - x2 * s, o2 = x1 * s + x2 * c;
-    if (hh < Hq) {
-      row[(int64_t)hh * D + i] = from_f<T>(o1);
-      row[(int64_t)hh * D + i + half] = from_f<T>(o2);
-    } else {
-      T *dst = k_new + ((int64_t)m * Hkv + (hh - Hq)) * D;
-      dst[i] = from_f<T>(o1);
-      dst[i + half] = from_f<T>(o2);
-    }
+  __shared__ float2 tab[kMaxHalf];
+  rope_table((float)pos[m], D, log2_base, tab);
+  const int half = D / 2, q4 = half / 4;
+  const int items = (Hq + Hkv) * q4;
+  for (int idx = threadIdx.x; idx < items; idx += blockDim.x) {
+    const int hh = idx / q4, i0 = (idx % q4) * 4;
+    float x1[4], x2[4], o1[4], o2[4];
+    load4(row + (int64_t)hh * D + i0, x1);
+    load4(row + (int64_t)hh * D + i0 + half, x2);
+    rope4(tab, i0, x1, x2, o1, o2);
+    T *dst = rope_dst(row, k_new, m, hh, Hq, Hkv, D);
+    store4(dst + i0, o1);
+    store4(dst + i0 + half, o2);
   }
   const uint4 *vsrc = reinterpret_cast<const uint4 *>(row + (int64_t)(Hq + Hkv) * D);
   uint4 *vdst = reinterpret_cast<uint4 *>(v_new + (int64_t)m * Hkv * D);
@@ -186,29 +231,29 @@ __global__ void splitk_rope_qkv_kernel(const float *part, int splits, int64_t pl
   const int m = blockIdx.x;
   T *row = qkv + (int64_t)m * ld;
   const float *prow = part + (int64_t)m * n;
-  const float p = (float)pos[m];
-  const int half = D / 2;
-  const int pairs = (Hq + Hkv) * half;
-  auto val = [&](int col) {
-    float a = prow[col];
-    for (int s = 1; s < splits; ++s) a += prow[s * plane + col];
-    return cf::to_float(from_f<T>(a));
-  };
-  for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
-    const int hh = idx / half, i = idx % half;
-    const float inv_freq = exp2f(-((float)(2 * i) / (float)D) * log2_base);
-    float s, c;
-    sincosf(p * inv_freq, &s, &c);
-    const float x1 = val(hh * D + i), x2 = val(hh * D + i + half);
-    const float o1 = x1 * c - x2 * s, o2 = x1 * s + x2 * c;
-    if (hh < Hq) {
-      row[(int64_t)hh * D + i] = from_f<T>(o1);
-      row[(int64_t)hh * D + i + half] = from_f<T>(o2);
-    } else {
-      T *dst = k_new + ((int64_t)m * Hkv + (hh - Hq)) * D;
-      dst[i] = from_f<T>(o1);
-      dst[i + half] = from_f<T>(o2);
+  __shared__ float2 tab[kMaxHalf];
+  rope_table((float)pos[m], D, log2_base, tab);
+  const int half = D / 2, q4 = half / 4;
+  const int items = (Hq + Hkv) * q4;
+  // four GEMM outputs at column col, reduced in split order and rounded to T
+  auto val4 = [&](int col, float (&o)[4]) {
+    float4 a = *reinterpret_cast<const float4 *>(prow + col);
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 c = *reinterpret_cast<const float4 *>(prow + sp * plane + col);
+      a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
     }
+    o[0] = cf::to_float(from_f<T>(a.x)); o[1] = cf::to_float(from_f<T>(a.y));
+    o[2] = cf::to_float(from_f<T>(a.z)); o[3] = cf::to_float(from_f<T>(a.w));
+  };
+  for (int idx = threadIdx.x; idx < items; idx += blockDim.x) {
+    const int hh = idx / q4, i0 = (idx % q4) * 4;
+    float x1[4], x2[4], o1[4], o2[4];
+    val4(hh * D + i0, x1);
+    val4(hh * D + i0 + half, x2);
+    rope4(tab, i0, x1, x2, o1, o2);
+    T *dst = rope_dst(row, k_new, m, hh, Hq, Hkv, D);
+    store4(dst + i0, o1);
+    store4(dst + i0 + half, o2);
   }
   T *vdst = v_new + (int64_t)m * Hkv * D;
   const int v0 = (Hq + Hkv) * D;
@@ -282,9 +327,9 @@ extern "C" int cf_rmsnorm(const void *x, int64_t ldx, const void *w, void *out, 
 extern "C" int cf_rope_qkv(void *qkv, int64_t ld, int32_t m, int32_t num_q_heads, int32_t num_kv_heads,
                            int32_t head_dim, const int32_t *pos, float base, void *k_new, void *v_new, int32_t dtype,
                            void *stream) {
-  if (m < 0 || head_dim % 16 || num_q_heads <= 0 || num_kv_heads <= 0 || !qkv || !pos || !k_new || !v_new)
+  if (m < 0 || head_dim % 16 || head_dim > 2 * kMaxHalf || num_q_heads <= 0 || num_kv_heads <= 0 || !qkv || !pos || !k_new || !v_new)
     return CF_EINVAL;
-  if (ld % 8 || !aligned16(qkv) || !aligned16(v_new) || !(base > 1.0f)) return CF_EINVAL;
+  if (ld % 8 || !aligned16(qkv) || !aligned16(k_new) || !aligned16(v_new) || !(base > 1.0f)) return CF_EINVAL;
   if (m == 0) return CF_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const float lb = log2f(base);
@@ -340,10 +385,11 @@ extern "C" int cf_splitk_rmsnorm(const float *partials, int32_t splits, int32_t 
 extern "C" int cf_splitk_rope_qkv(const float *partials, int32_t splits, int32_t m, void *qkv, int64_t ld,
                                   int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const int32_t *pos,
                                   float base, void *k_new, void *v_new, int32_t dtype, void *stream) {
-  if (m < 0 || splits < 1 || head_dim % 16 || num_q_heads <= 0 || num_kv_heads <= 0 || !partials || !qkv || !pos ||
-      !k_new || !v_new)
+  if (m < 0 || splits < 1 || head_dim % 16 || head_dim > 2 * kMaxHalf || num_q_heads <= 0 || num_kv_heads <= 0 ||
+      !partials || !qkv || !pos || !k_new || !v_new)
     return CF_EINVAL;
-  if (ld % 8 || !aligned16(partials) || !aligned16(qkv) || !aligned16(v_new) || !(base > 1.0f)) return CF_EINVAL;
+  if (ld % 8 || !aligned16(partials) || !aligned16(qkv) || !aligned16(k_new) || !aligned16(v_new) || !(base > 1.0f))
+    return CF_EINVAL;
   if (m == 0) return CF_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const float lb = log2f(base);

@@ -67,6 +67,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait whose hardware suspension ends after at most `hint_ns` (the phase
+// completing ends it earlier).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -96,10 +110,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
 // Suspending variant: try_wait parks the thread in hardware until the phase
 // completes (or a hint expires) instead of spinning on issue slots.
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+  // the suspension hint never exceeds the limit, so a short limit is observed too
+  const uint32_t hint = limit_ns < 0xffffffffull ? (uint32_t)limit_ns : 0xffffffffu;
+  if (mbar_try_wait_hint(bar, parity, hint)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_hint(bar, parity, hint)) return true;
     if (globaltimer() - t0 > limit_ns) return false;
   }
 }

@@ -422,7 +422,8 @@ int cf_rmsnorm(const void *x, int64_t ldx, const void *w, void *out, int64_t ldo
  * o1 = x1 c - x2 s, o2 = x1 s + x2 c; angle = pos * base^(-2i/D)) on the
  * fused QKV rows qkv[m][(Hq + 2 Hkv) * D] (m = b*R + r, position pos[m]):
  * q is rotated in place; rotated k and plain v go to k_new / v_new
- * [B][R][Hkv][D] (this layer's slice). */
+ * [B][R][Hkv][D] (this layer's slice).  D a multiple of 16, at most 256;
+ * qkv, k_new and v_new 16-byte aligned. */
 int cf_rope_qkv(void *qkv, int64_t ld, int32_t m, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                 const int32_t *pos, float base, void *k_new, void *v_new, int32_t dtype, void *stream);
 /* SwiGLU: out[m, j] = silu(gu[m, j]) * gu[m, ffn + j] */

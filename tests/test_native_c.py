@@ -236,3 +236,31 @@ def test_reference_engine_py_runs_unchanged():
                 sys.modules.pop(k, None)
             else:
                 sys.modules[k] = v
+
+
+@pytest.mark.gpu
+def test_verify_batch_on_gpu_uses_the_engine_stream():
+    """The batched entry point runs the GPU acceptance kernel with uniforms
+    drawn from the engine's own stream (sequence-major); fed the kernel's
+    exported probabilities and those uniforms, the oracle decides identically."""
+    import torch
+    B, K, V = 16, 4, 5000
+    g = torch.Generator().manual_seed(2)
+    d = torch.randn(B, K + 1, V, generator=g) * 2
+    t = d + 0.4 * torch.randn(B, K + 1, V, generator=g)
+    dt = torch.multinomial(torch.softmax(d[:, :K].reshape(-1, V), -1), 1, generator=g).reshape(B, K).to(torch.int32)
+    cfg = _C.SpeculativeConfig()
+    cfg.rng_seed = 77
+    eng = _C.SpeculativeEngine(cfg)
+    res = eng.verify_batch(d[:, :K].cuda(), t.cuda(), dt.cuda(), eos_token_id=-1, export_probs=True)
+    torch.cuda.synchronize()
+    u = oracle.ref_uniforms(77, B * (K + 1)).reshape(B, K + 1) if oracle.ref_available() else None
+    if u is not None:
+        tok, na, _ = oracle.accept(dt.numpy(), res.probs_draft.cpu().numpy(), res.probs_target.cpu().numpy(), u, -1)
+        assert (res.num_accepted.cpu().numpy() == na).all()
+        for b in range(B):
+            assert res.emitted(b) == tok[b, : na[b] + 1].tolist()
+    # the block of B*(K+1) draws was consumed: the next draw continues the stream
+    nxt = eng.draw_uniforms(1)
+    if oracle.ref_available():
+        assert nxt[0] == oracle.ref_uniforms(77, B * (K + 1) + 1)[-1]
