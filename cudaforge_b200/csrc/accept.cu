@@ -283,18 +283,20 @@ __device__ __forceinline__ IncMap block_exclusive_scan(IncMap x, ScanShared &sh)
   return compose(sh.warp_pre[w], lex);
 }
 
-// Sequential fp32 accumulation of the values v_0..v_{V-1} (all >= 0 or
-// NaN/Inf) that f(i0, out[8]) produces eight at a time.
-// SEARCH == false: returns the total (the reference's `sum`).
-// SEARCH == true : *hit = the first i with r <= cum_i, or V-1.
+// Sequential fp32 accumulation cum += v_i for i in [lo, hi), starting from the
+// exact value c0, of the values (all >= 0 or NaN/Inf) that f(i0, out[8])
+// produces eight at a time.  Returns the running value after the range (or
+// after the hit / the first NaN / Inf, which ends the chain: nothing later
+// can match or change a NaN, and an Inf is final for the searches here).
+// SEARCH: *hit = the first i in the range with r <= cum_i, else -1.
 template <bool SEARCH, class F>
-__device__ float exact_chain(F f, int64_t V, float r, int64_t *hit, ScanShared &sh) {
+__device__ float exact_chain_range(F f, int64_t lo, int64_t hi, float c0, float r, int64_t *hit, ScanShared &sh) {
   const int tid = threadIdx.x;
-  if (tid == 0) { sh.c = 0.0f; sh.done = 0; }
+  if (tid == 0) { sh.c = c0; sh.done = 0; }
   __syncthreads();
   int64_t result = -1;
-  for (int64_t base = 0; base < V; base += kScanChunk) {
-    const int n = (int)((V - base) < kScanChunk ? (V - base) : kScanChunk);
+  for (int64_t base = lo; base < hi; base += kScanChunk) {
+    const int n = (int)((hi - base) < kScanChunk ? (hi - base) : kScanChunk);
     float v[kPerThread];
 #pragma unroll
     for (int j = 0; j < kPerThread; j += 8) {
@@ -386,7 +388,17 @@ __device__ float exact_chain(F f, int64_t V, float r, int64_t *hit, ScanShared &
   }
   const float total = sh.c;
   __syncthreads();
-  if (SEARCH) *hit = result >= 0 ? result : V - 1;
+  if (SEARCH) *hit = result;
+  return total;
+}
+
+// The whole row from 0: SEARCH falls back to V-1 when r is never reached
+// (speculative.cpp:23).
+template <bool SEARCH, class F>
+__device__ float exact_chain(F f, int64_t V, float r, int64_t *hit, ScanShared &sh) {
+  int64_t h = -1;
+  const float total = exact_chain_range<SEARCH>(f, 0, V, 0.0f, r, &h, sh);
+  if (SEARCH) *hit = h >= 0 ? h : V - 1;
   return total;
 }
 
@@ -544,6 +556,361 @@ decide_kernel(cf_accept_args a, float c, const RowStat *stats) {
     a.out_num_accepted[b] = s_na;
     a.out_eos[b] = (tok == a.eos_token_id);
   }
+}
+
+// ---------------------------------------------------------------------------
+// The stochastic draw across many CTAs.
+//
+// The single-CTA chain above walks a row chunk after chunk; here every row is
+// cut into kNch chunks and the chunks are worked on by separate CTAs:
+//   prep_kernel     grid (kNch, B): the K acceptance tests (every CTA of a
+//                   sequence evaluates them; block 0 publishes the outcome)
+//                   and, per chunk, approximate sums of the values the draw
+//                   will accumulate (any order: they only predict);
+//   maps_kernel     grid (kNch, B): per chunk, the composed increment map of
+//                   the whole chunk on the ulp grid of the binade its start
+//                   value is PREDICTED to lie in (from the approximate sums);
+//   resolve_kernel  grid (B): walks the chunks with the exact running value:
+//                   a chunk whose start really lies on the predicted grid and
+//                   whose end stays inside that binade is applied in O(1)
+//                   from its map; any other chunk (the first, those where a
+//                   binade is crossed, a wrong prediction, NaN / Inf) and the
+//                   chunk holding the search hit are scanned exactly.
+// The running value is exact at every chunk boundary, so the result is the
+// same bit for bit as the sequential loop.  Stage 0 is the residual mass (or
+// directly the bonus draw), stage 1 the residual draw.
+// ---------------------------------------------------------------------------
+constexpr int kNch = 32;
+constexpr int kChainThreads = 256;
+constexpr int kNoMap = INT_MIN;
+constexpr int kSerial = 512;  // the first elements of a row cross many binades: done serially
+
+struct SeqState {
+  int mode;    // -1 bad draft token, kDone, kResidual, kBonus
+  int row;     // the row of the draw (rejected position, or K for the bonus)
+  int na;      // accepted drafts
+  float r;     // the draw's uniform
+  float sum;   // stage 0 result: exact residual mass
+  int vkind;   // stage 1 values: 1 = residual / sum, 2 = target row (mass <= 1e-6)
+  int pad[2];
+};
+
+struct ChunkInfo {
+  float approx[2];  // approximate chunk sums: [0] stage-0 values, [1] target probabilities (residual mode)
+  int ue, me, mo;   // the chunk's composed map on the grid 2^ue (kNoMap: scan it)
+  int pad[3];
+};
+
+__host__ __device__ inline size_t accept_stats_bytes(int64_t batch, int64_t k) {
+  return ((size_t)batch * (2 * (size_t)k + 1) * sizeof(RowStat) + 255) & ~(size_t)255;
+}
+
+__device__ __forceinline__ void chunk_range(int64_t V, int j, int64_t &lo, int64_t &hi) {
+  const int64_t cl = ((V + kNch - 1) / kNch + 7) & ~(int64_t)7;
+  lo = (int64_t)j * cl;
+  hi = lo + cl < V ? lo + cl : V;
+}
+
+// Fixed-order block sum (kChainThreads threads): warp butterflies, then warp
+// results in warp order.
+__device__ __forceinline__ float block_sum256(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.0f;
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kChainThreads / 32; ++i) t += red[i];
+  return t;  // valid in thread 0
+}
+
+// The values a chain accumulates, eight at a time, for sequence b:
+//   kind 0: target probabilities of `row`
+//   kind 1: residual max(0, p - q) of `row`
+//   kind 2: residual / sum
+template <typename T>
+struct ChainVals {
+  const T *xt, *xd;
+  RowStat st_t, st_d;
+  float c, sum;
+  int64_t V;
+  int kind;
+  __device__ __forceinline__ void operator()(int64_t i0, float (&o)[8]) const {
+    load8<T>(xt, i0, V, o);
+    if (kind == 0) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] = prob_of(o[q], c, st_t);
+      return;
+    }
+    float d8[8];
+    load8<T>(xd, i0, V, d8);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float d = __fsub_rn(prob_of(o[q], c, st_t), prob_of(d8[q], c, st_d));
+      o[q] = d > 0.0f ? d : 0.0f;  // std::max(0.0f, d)
+      if (kind == 2) o[q] = __fdiv_rn(o[q], sum);
+    }
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ ChainVals<T> chain_vals(const cf_accept_args &a, float c, const RowStat *st, int b, int row,
+                                                   int kind, float sum) {
+  const int K = a.k;
+  ChainVals<T> f;
+  f.xt = row_ptr<T>(a.target_logits, a.target_seq_stride, a.target_row_stride, b, row);
+  f.xd = kind == 0 ? f.xt : row_ptr<T>(a.draft_logits, a.draft_seq_stride, a.draft_row_stride, b, row);
+  f.st_t = st[K + row];
+  f.st_d = kind == 0 ? f.st_t : st[row];
+  f.c = c;
+  f.sum = sum;
+  f.V = a.vocab;
+  f.kind = kind;
+  return f;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kChainThreads)
+prep_kernel(cf_accept_args a, float c, const RowStat *stats, SeqState *seq, ChunkInfo *ci) {
+  __shared__ float s_ratio[64];
+  __shared__ int s_mode, s_row, s_na;
+  __shared__ float s_r, red[kChainThreads / 32];
+  const int j = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int K = a.k;
+  const int64_t V = a.vocab;
+  const RowStat *st = stats + (int64_t)b * (2 * K + 1);
+  const int32_t *dt = a.draft_tokens + (int64_t)b * K;
+  auto ratio_of = [&](int i) -> float {  // speculative.cpp:69-74; NaN marks a bad draft token
+    const int32_t tok = dt[i];
+    if (tok < 0 || tok >= V) return __int_as_float(0x7fffffff);
+    const T *xd = row_ptr<T>(a.draft_logits, a.draft_seq_stride, a.draft_row_stride, b, i);
+    const T *xt = row_ptr<T>(a.target_logits, a.target_seq_stride, a.target_row_stride, b, i);
+    const float q = prob_of(cf::to_float(xd[tok]), c, st[i]);
+    const float p = prob_of(cf::to_float(xt[tok]), c, st[K + i]);
+    const float pq = __fdiv_rn(p, q);
+    return (q > 0.0f) ? ((pq < 1.0f) ? pq : 1.0f) : 0.0f;
+  };
+  for (int i = tid; i < K && i < 64; i += kChainThreads) s_ratio[i] = ratio_of(i);
+  __syncthreads();
+  if (tid == 0) {
+    // speculative.cpp:66-101: the tests in order, one uniform each
+    const float *u = a.uniforms + (int64_t)b * (K + 1);
+    int32_t *out = a.out_tokens + (int64_t)b * (K + 1);
+    int na = 0, used = 0, mode = kBonus, row = K;
+    for (int i = 0; i < K; ++i) {
+      const float ratio = i < 64 ? s_ratio[i] : ratio_of(i);
+      if (isnan(ratio)) { mode = -1; break; }
+      const float r = u[used++];
+      if (r <= ratio) {
+        const int32_t tok = dt[i];
+        if (j == 0) out[na] = tok;
+        ++na;
+        if (tok == a.eos_token_id) { mode = kDone; break; }
+      } else {
+        mode = kResidual;
+        row = i;
+        break;
+      }
+    }
+    s_mode = mode;
+    s_row = row;
+    s_na = na;
+    s_r = (mode == kDone || mode < 0) ? 0.0f : u[used];
+    if (j == 0) {
+      SeqState sq{};
+      sq.mode = mode; sq.row = row; sq.na = na; sq.r = s_r; sq.sum = 0.0f; sq.vkind = 0;
+      seq[b] = sq;
+      if (mode < 0) { a.out_num_accepted[b] = -1; a.out_eos[b] = 0; }
+      if (mode == kDone) { out[na] = a.eos_token_id; a.out_num_accepted[b] = na; a.out_eos[b] = 1; }
+    }
+  }
+  __syncthreads();
+  const int mode = s_mode;
+  if (mode == kDone || mode < 0) return;
+  int64_t lo, hi;
+  chunk_range(V, j, lo, hi);
+  const ChainVals<T> f = chain_vals<T>(a, c, st, b, s_row, mode == kResidual ? 1 : 0, 0.0f);
+  const ChainVals<T> fp = chain_vals<T>(a, c, st, b, s_row, 0, 0.0f);
+  float s0 = 0.0f, s1 = 0.0f;
+  for (int64_t i0 = lo + (int64_t)tid * 8; i0 < hi; i0 += (int64_t)kChainThreads * 8) {
+    float v[8];
+    f(i0, v);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (i0 + q < hi) s0 += v[q];
+    if (mode == kResidual) {
+      fp(i0, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (i0 + q < hi) s1 += v[q];
+    }
+  }
+  s0 = block_sum256(s0, red);
+  s1 = block_sum256(s1, red);
+  if (tid == 0) {
+    ci[(int64_t)b * kNch + j].approx[0] = s0;
+    ci[(int64_t)b * kNch + j].approx[1] = s1;
+  }
+}
+
+// The chain a sequence runs in stage STAGE: kind of values (-1: none) and
+// whether it searches.
+__device__ __forceinline__ int chain_kind(const SeqState &sq, int stage, bool &search) {
+  search = true;
+  if (stage == 0) {
+    if (sq.mode == kBonus) return 0;
+    if (sq.mode == kResidual) { search = false; return 1; }
+    return -1;
+  }
+  if (sq.mode != kResidual) return -1;
+  return sq.vkind == 2 ? 0 : 2;
+}
+
+template <typename T, int STAGE>
+__global__ void __launch_bounds__(kChainThreads)
+maps_kernel(cf_accept_args a, float c, const RowStat *stats, const SeqState *seq, ChunkInfo *ci) {
+  __shared__ int s_ue;
+  __shared__ IncMap s_w[kChainThreads / 32];
+  const int j = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const SeqState sq = seq[b];
+  bool search;
+  const int kind = chain_kind(sq, STAGE, search);
+  if (kind < 0) return;
+  ChunkInfo *info = ci + (int64_t)b * kNch;
+  if (j == 0) {  // a row's first chunk always starts at 0 and is scanned
+    if (tid == 0) info[0].ue = kNoMap;
+    return;
+  }
+  const int64_t V = a.vocab;
+  int64_t lo, hi;
+  chunk_range(V, j, lo, hi);
+  if (lo >= hi) return;
+  if (tid == 0) {
+    // predicted start value: approximate sums of the chunks before this one
+    const int idx = (STAGE == 1 && kind == 0) ? 1 : 0;
+    float pre = 0.0f;
+    for (int i = 0; i < j; ++i) pre += info[i].approx[idx];
+    if (STAGE == 1 && kind == 2) pre = pre / sq.sum;
+    int C;
+    grid_of(pre, C, s_ue);
+  }
+  __syncthreads();
+  const int ue = s_ue;
+  const RowStat *st = stats + (int64_t)b * (2 * a.k + 1);
+  const ChainVals<T> f = chain_vals<T>(a, c, st, b, sq.row, kind, sq.sum);
+  // thread t owns the contiguous elements [lo + t*per, lo + (t+1)*per): maps compose in thread order
+  const int64_t per = ((hi - lo + kChainThreads - 1) / kChainThreads + 7) & ~(int64_t)7;
+  IncMap m{0, 0};
+  for (int64_t i0 = lo + tid * per; i0 < lo + (tid + 1) * per && i0 < hi; i0 += 8) {
+    float v[8];
+    f(i0, v);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (i0 + q < hi) m = compose(m, elem_map(v[q], ue));
+  }
+  // in-order composition across the warp (lane l holds [l, l + 2o) after step o), then across warps
+  const int lane = tid & 31, w = tid >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    IncMap y;
+    y.e = __shfl_down_sync(0xffffffffu, m.e, o);
+    y.o = __shfl_down_sync(0xffffffffu, m.o, o);
+    if ((lane & (2 * o - 1)) == 0 && lane + o < 32) m = compose(m, y);
+  }
+  if (lane == 0) s_w[w] = m;
+  __syncthreads();
+  if (tid == 0) {
+    IncMap t{0, 0};
+    for (int i = 0; i < kChainThreads / 32; ++i) t = compose(t, s_w[i]);
+    info[j].ue = ue;
+    info[j].me = t.e;
+    info[j].mo = t.o;
+  }
+}
+
+template <typename T, int STAGE>
+__global__ void __launch_bounds__(kScanThreads, 1)
+resolve_kernel(cf_accept_args a, float c, const RowStat *stats, SeqState *seq, const ChunkInfo *ci) {
+  __shared__ ScanShared sh;
+  __shared__ int s_ue[kNch], s_me[kNch], s_mo[kNch];
+  __shared__ float s_buf[kSerial];
+  __shared__ float s_cum;
+  __shared__ long long s_hit;
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const SeqState sq = seq[b];
+  bool search;
+  const int kind = chain_kind(sq, STAGE, search);
+  if (kind < 0) return;
+  const int64_t V = a.vocab;
+  const RowStat *st = stats + (int64_t)b * (2 * a.k + 1);
+  const ChainVals<T> f = chain_vals<T>(a, c, st, b, sq.row, kind, sq.sum);
+  for (int i = tid; i < kNch; i += kScanThreads) {
+    s_ue[i] = ci[(int64_t)b * kNch + i].ue;
+    s_me[i] = ci[(int64_t)b * kNch + i].me;
+    s_mo[i] = ci[(int64_t)b * kNch + i].mo;
+  }
+  const float r = search ? sq.r : 0.0f;
+  // the first kSerial elements: one thread, the reference's loop itself
+  const int64_t n0 = V < kSerial ? V : kSerial;
+  for (int64_t i0 = (int64_t)tid * 8; i0 < n0; i0 += (int64_t)kScanThreads * 8) {
+    float v[8];
+    f(i0, v);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (i0 + q < n0) s_buf[i0 + q] = v[q];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float cum = 0.0f;
+    long long hit = -1;
+    for (int i = 0; i < n0; ++i) {
+      cum = __fadd_rn(cum, s_buf[i]);
+      if (search && r <= cum) { hit = i; break; }
+    }
+    s_cum = cum;
+    s_hit = hit;
+  }
+  __syncthreads();
+  float cum = s_cum;
+  int64_t hit = s_hit;
+  for (int j = 0; j < kNch && hit < 0 && isfinite(cum); ++j) {
+    int64_t lo, hi;
+    chunk_range(V, j, lo, hi);
+    if (lo >= V) break;
+    const bool whole = lo >= n0;  // the chunk's map covers it only if the serial prefix did not
+    if (!whole) lo = n0;
+    if (lo >= hi) continue;
+    bool fast = false;
+    float end = 0.0f;
+    if (whole && s_ue[j] != kNoMap) {
+      int C, ue;
+      grid_of(cum, C, ue);
+      if (ue == s_ue[j]) {
+        const int Ce = apply(IncMap{s_me[j], s_mo[j]}, C);
+        if (Ce < kTop) { fast = true; end = ldexpf((float)Ce, ue); }
+      }
+    }
+    if (fast && !(search && r <= end)) { cum = end; continue; }
+    // scan the chunk exactly from its exact start value (and find the hit, searching)
+    int64_t h = -1;
+    if (search) cum = exact_chain_range<true>(f, lo, hi, cum, r, &h, sh);
+    else cum = exact_chain_range<false>(f, lo, hi, cum, r, nullptr, sh);
+    hit = h;
+  }
+  if (tid != 0) return;
+  if (!search) {  // residual mass: speculative.cpp:34-41
+    SeqState o = sq;
+    o.sum = cum;
+    o.vkind = (cum <= 1e-6f) ? 2 : 1;
+    seq[b] = o;
+    return;
+  }
+  const int64_t tok = hit >= 0 ? hit : V - 1;
+  a.out_tokens[(int64_t)b * (a.k + 1) + sq.na] = (int32_t)tok;
+  a.out_num_accepted[b] = sq.na;
+  a.out_eos[b] = (tok == a.eos_token_id);
 }
 
 // ---------------------------------------------------------------------------
@@ -715,7 +1082,19 @@ int launch_accept(const cf_accept_args &a, cudaStream_t stream) {
   dim3 g1(2 * a.k + 1, a.batch);
   row_stats_kernel<T><<<g1, kStatsThreads, 0, stream>>>(a, c, stats, a.k, a.k + 1);
   if (a.probs_draft || a.probs_target) export_probs_kernel<T><<<g1, 256, 0, stream>>>(a, c, stats, a.k, a.k + 1);
-  decide_kernel<T><<<a.batch, kDecideThreads, 0, stream>>>(a, c, stats);
+  if (a.greedy) {
+    decide_kernel<T><<<a.batch, kDecideThreads, 0, stream>>>(a, c, stats);
+    return cf_launch_status();
+  }
+  uint8_t *base = reinterpret_cast<uint8_t *>(a.workspace) + accept_stats_bytes(a.batch, a.k);
+  SeqState *seq = reinterpret_cast<SeqState *>(base);
+  ChunkInfo *ci = reinterpret_cast<ChunkInfo *>(base + (size_t)a.batch * sizeof(SeqState));
+  const dim3 gc(kNch, a.batch);
+  prep_kernel<T><<<gc, kChainThreads, 0, stream>>>(a, c, stats, seq, ci);
+  maps_kernel<T, 0><<<gc, kChainThreads, 0, stream>>>(a, c, stats, seq, ci);
+  resolve_kernel<T, 0><<<a.batch, kScanThreads, 0, stream>>>(a, c, stats, seq, ci);
+  maps_kernel<T, 1><<<gc, kChainThreads, 0, stream>>>(a, c, stats, seq, ci);
+  resolve_kernel<T, 1><<<a.batch, kScanThreads, 0, stream>>>(a, c, stats, seq, ci);
   return cf_launch_status();
 }
 
@@ -780,7 +1159,7 @@ extern "C" int cf_accept_tree(const cf_accept_tree_args *t, void *stream) {
 
 extern "C" size_t cf_accept_workspace_bytes(int32_t batch, int32_t k) {
   if (batch < 0 || k < 0) return 0;
-  return (size_t)batch * (2 * (size_t)k + 1) * sizeof(RowStat);
+  return accept_stats_bytes(batch, k) + (size_t)batch * (sizeof(SeqState) + kNch * sizeof(ChunkInfo));
 }
 
 extern "C" int cf_accept_sample(const cf_accept_args *args, void *stream) {
@@ -808,14 +1187,14 @@ extern "C" int cf_accept_sample(const cf_accept_args *args, void *stream) {
 // Allocation-free variant.  Some callers cannot allocate device memory at
 // all: code running where cudaMalloc is off limits (an allocator hook, a
 // host runtime that owns every byte of device memory, a plugin that may only
-// touch the buffers it is handed).  For them the per-row softmax statistics
-// live in a fixed array inside this library instead of a caller workspace.
-// The array is kAcceptScratchRows RowStats (512 KiB) on every GPU that loads
-// the library, held until the process exits.
+// touch the buffers it is handed).  For them the acceptance scratch (row
+// statistics, per-sequence state, per-chunk maps) lives in a fixed 2 MiB
+// array inside this library instead of a caller workspace, on every GPU that
+// loads the library, held until the process exits.
 // ---------------------------------------------------------------------------
 namespace {
-constexpr int kAcceptScratchRows = 65536;  // batch * (2k + 1) must not exceed this
-static __device__ __align__(256) RowStat g_accept_scratch[kAcceptScratchRows];
+constexpr size_t kAcceptScratchBytes = size_t(2) << 20;  // cf_accept_workspace_bytes(batch, k) must fit
+static __device__ __align__(256) uint8_t g_accept_scratch[kAcceptScratchBytes];
 
 constexpr int kMaxDevices = 64;
 void *g_scratch_ptr[kMaxDevices];
@@ -840,13 +1219,14 @@ int scratch_ptr(void **out) {
 extern "C" int cf_accept_sample_noalloc(const cf_accept_args *args, void *stream) {
   if (!args) return CF_EINVAL;
   if (args->batch < 0 || args->k < 0) return CF_EINVAL;
-  if ((int64_t)args->batch * (2 * (int64_t)args->k + 1) > kAcceptScratchRows) return CF_ERANGE;
+  if (cf_accept_workspace_bytes(args->batch, args->k) > kAcceptScratchBytes) return CF_ERANGE;
   void *ws = nullptr;
   const int rc = scratch_ptr(&ws);
   if (rc != CF_OK) return rc;
   cf_accept_args a = *args;
-  a.workspace = ws;  // every row statistic is written before it is read: nothing to clear
+  // every scratch word a call reads was written earlier in that same call: nothing to clear
+  a.workspace = ws;
   return cf_accept_sample(&a, stream);
 }
 
-extern "C" int cf_accept_noalloc_max_rows(void) { return kAcceptScratchRows; }
+extern "C" size_t cf_accept_noalloc_max_bytes(void) { return kAcceptScratchBytes; }

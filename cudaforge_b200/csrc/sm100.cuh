@@ -110,8 +110,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
 // Suspending variant: try_wait parks the thread in hardware until the phase
 // completes (or a hint expires) instead of spinning on issue slots.
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
-  // the suspension hint never exceeds the limit, so a short limit is observed too
-  const uint32_t hint = limit_ns < 0xffffffffull ? (uint32_t)limit_ns : 0xffffffffu;
+  // A hardware suspension lasts a minimum quantum whatever the hint, so a limit
+  // below a millisecond is observed through the polling wait instead.
+  if (limit_ns < 1000000ull) return mbar_wait(bar, parity, limit_ns);
+  const uint32_t hint = 1000000u;  // ns; the phase completing ends a suspension earlier
   if (mbar_try_wait_hint(bar, parity, hint)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {

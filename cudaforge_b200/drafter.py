@@ -65,7 +65,8 @@ class BatchDrafter:
         self.res = AcceptResult(tokens=torch.zeros(B, 1, dtype=torch.int32, device=dev),
                                 num_accepted=torch.zeros(B, dtype=torch.int32, device=dev),
                                 eos=torch.zeros(B, dtype=torch.bool, device=dev))
-        self.ws = torch.empty(4096 + 16 * B, dtype=torch.uint8, device=dev)
+        from . import _lib as _l
+        self.ws = torch.empty(_l.lib().cf_accept_workspace_bytes(B, 0) + 256, dtype=torch.uint8, device=dev)
         from . import _lib
         self.st = _lib.DeviceStatus(dev)
         self.status = self.st.dev

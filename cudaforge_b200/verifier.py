@@ -56,7 +56,8 @@ class BatchVerifier:
         self.res = AcceptResult(tokens=torch.zeros(B, R, dtype=torch.int32, device=dev),
                                 num_accepted=torch.zeros(B, dtype=torch.int32, device=dev),
                                 eos=torch.zeros(B, dtype=torch.bool, device=dev))
-        self.ws = torch.empty(4096 + 16 * B * (2 * k + 1), dtype=torch.uint8, device=dev)
+        from . import _lib as _l
+        self.ws = torch.empty(_l.lib().cf_accept_workspace_bytes(B, k) + 256, dtype=torch.uint8, device=dev)
         from . import _lib
         self.st = _lib.DeviceStatus(dev)  # every kernel of the step records CF_ETIMEOUT / CF_ERANGE here
         self.status = self.st.dev

@@ -116,19 +116,20 @@ int cf_accept_sample(const cf_accept_args *args, void *stream);
 /* Same as cf_accept_sample, for callers that must not allocate device memory
  * (an allocator hook, a runtime that owns all device memory, a plugin limited
  * to the buffers it is given).  No counterpart in the reference.  args->workspace
- * is ignored: the row statistics go to a fixed array compiled into this
- * library (cf_accept_noalloc_max_rows() rows, 512 KiB per GPU that loads the
- * library, held until exit).  batch * (2k + 1) beyond that limit returns
- * CF_ERANGE and launches nothing.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture.  The address is cached per device ordinal for
- * the life of the process: after cudaDeviceReset (or any teardown of the
- * device's primary context) it is stale, so do not call this entry point
- * again in that process.  All calls share the array: calls that can run
- * at the same time on the GPU (different streams, different host threads)
- * race and must be serialised by the caller.  No cudaMalloc / cudaFree. */
+ * is ignored: the scratch goes to a fixed array compiled into this library
+ * (cf_accept_noalloc_max_bytes() = 2 MiB per GPU that loads the library, held
+ * until exit).  A call whose cf_accept_workspace_bytes(batch, k) exceeds that
+ * returns CF_ERANGE and launches nothing (K = 5: up to 1,833 sequences).  The
+ * first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * The address is cached per device ordinal for the life of the process: after
+ * cudaDeviceReset (or any teardown of the device's primary context) it is
+ * stale, so do not call this entry point again in that process.  All calls
+ * share the array: calls that can run at the same time on the GPU (different
+ * streams, different host threads) race and must be serialised by the caller.
+ * No cudaMalloc / cudaFree. */
 int cf_accept_sample_noalloc(const cf_accept_args *args, void *stream);
-int cf_accept_noalloc_max_rows(void);
+size_t cf_accept_noalloc_max_bytes(void);
 
 /* ------------------------------------------------------------------------
  * Tree acceptance.  The reference has no tree verifier; this extends

@@ -16,7 +16,8 @@ def test_status_strings_and_workspace_query():
     L = _lib.lib()
     assert L.cf_status_string(0) == b"CF_OK"
     assert b"EINVAL" in L.cf_status_string(-1)
-    assert L.cf_accept_workspace_bytes(64, 5) == 64 * 11 * 8
+    # row statistics (8 B per row, padded to 256 B) + per sequence 32 B of state and 32 chunk records of 32 B
+    assert L.cf_accept_workspace_bytes(64, 5) == ((64 * 11 * 8 + 255) // 256) * 256 + 64 * (32 + 32 * 32)
 
 
 def test_accept_rejects_bad_args_on_host():

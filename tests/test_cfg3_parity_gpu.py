@@ -63,12 +63,18 @@ def test_cfg3_graph_step_logits_and_acceptance():
     scale = max(1.0, ref.abs().max().item())
     err = (logits.float() - ref).abs().max().item() / scale
     top2 = ref.topk(2, dim=-1).values
-    clear = (top2[..., 0] - top2[..., 1]) > 2e-2 * scale
+    margin = top2[..., 0] - top2[..., 1]
+    clear = margin > 2e-2 * scale
+    # rows whose fp32 top-2 margin exceeds twice the measured max error must agree
+    decisive = margin > 2.0 * err * scale
     agree = logits.float().argmax(-1) == ref.argmax(-1)
-    print(f"cfg3 logits: max-abs/scale {err:.3e} (scale {scale:.3f}), argmax agreement "
-          f"{agree.float().mean().item():.4f} of {agree.numel()} rows, {int(clear.sum())} rows with a clear margin")
+    print(f"cfg3 logits: max-abs/scale {err:.3e} (scale {scale:.3f}); argmax agreement "
+          f"{agree.float().mean().item():.4f} of {agree.numel()} rows, "
+          f"{agree[decisive].float().mean().item() if decisive.any() else float('nan'):.4f} of "
+          f"{int(decisive.sum())} rows with a top-2 margin > 2x the max error, {int(clear.sum())} rows with a "
+          f"margin > the tolerance")
     assert err <= 2e-2, err
-    assert agree[clear].all()
+    assert agree[clear].all() and agree[decisive].all()
 
     # acceptance: graph step == eager kernel == oracle on the exported probabilities
     eager = accept_sample(dlog, logits, dtok, uni[1], export_probs=True)

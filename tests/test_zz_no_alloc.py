@@ -51,7 +51,7 @@ def _inputs(seed, B, K, V):
 
 def test_noalloc_matches_regular_entry_point_twice():
     for call, (seed, B, K, V, T, greedy) in enumerate([(1, 16, 5, 32000, 1.0, False), (2, 9, 3, 4099, 0.8, False),
-                                                         (3, 5, 4, 1000, 1.0, True)]):
+                                                         (3, 5, 4, 1000, 1.0, True), (4, 64, 5, 128256, 1.0, False)]):
         d, t, dt, u = _inputs(seed, B, K, V)
         eos = int(dt[0, 0])
         ref = accept_sample(d, t, dt, None if greedy else u, temperature=T, eos_token_id=eos, greedy=greedy)
@@ -66,8 +66,11 @@ def test_noalloc_matches_regular_entry_point_twice():
 def test_noalloc_rejects_oversized_batch():
     L = _lib.lib()
     L.cf_accept_sample_noalloc.argtypes = [ctypes.POINTER(_lib.CfAcceptArgs), ctypes.c_void_p]
-    rows = L.cf_accept_noalloc_max_rows()
+    L.cf_accept_noalloc_max_bytes.restype = ctypes.c_size_t
+    cap = L.cf_accept_noalloc_max_bytes()
     K = 5
-    B = rows // (2 * K + 1) + 1
+    B = 1
+    while L.cf_accept_workspace_bytes(B, K) <= cap:
+        B *= 2
     a = _lib.CfAcceptArgs(batch=B, k=K, vocab=10)
     assert L.cf_accept_sample_noalloc(ctypes.byref(a), None) == _lib.CF_ERANGE
