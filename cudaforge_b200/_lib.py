@@ -31,7 +31,7 @@ class CfAcceptArgs(ctypes.Structure):
         ("draft_tokens", _P), ("uniforms", _P), ("temperature", _F32),
         ("eos_token_id", _I32), ("greedy", _I32),
         ("out_tokens", _P), ("out_num_accepted", _P), ("out_eos", _P),
-        ("workspace", _P), ("probs_draft", _P), ("probs_target", _P),
+        ("workspace", _P), ("probs_draft", _P), ("probs_target", _P), ("top_p", _F32),
     ]
 
 

@@ -59,12 +59,16 @@ def accept_sample(
     workspace: Optional[torch.Tensor] = None,
     out: Optional[AcceptResult] = None,
     stream: Optional[torch.cuda.Stream] = None,
+    top_p: Optional[float] = None,
 ) -> AcceptResult:
     """Run the fused acceptance kernel.
 
     draft_logits [B, K, V] and target_logits [B, K+1, V] (fp32 / bf16 / fp16,
     same dtype, on one CUDA device), draft_tokens [B, K] (int32/int64),
     uniforms [B, K+1] fp32 in [0, 1) (required unless greedy).
+    top_p in (0, 1) applies the nucleus filter of the reference Python engine
+    (speculative.py:58-84, :188-195) to the bonus draw (all K accepted); None
+    (default) follows the reference C++ verifier, which has no top-p.
     Raises ValueError on shape mismatch, as the reference raises
     std::invalid_argument (speculative.cpp:59-62).
     """
@@ -121,11 +125,14 @@ def accept_sample(
         out_eos=out.eos.data_ptr(), workspace=workspace.data_ptr(),
         probs_draft=out.probs_draft.data_ptr() if export_probs else None,
         probs_target=out.probs_target.data_ptr() if export_probs else None,
+        top_p=float(top_p) if top_p is not None else 0.0,
     )
     s = stream if stream is not None else torch.cuda.current_stream(dev)
     with torch.cuda.device(dev):
         _lib.check(L.cf_accept_sample(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), "cf_accept_sample")
-    _lib.count(3 if export_probs else 2)
+    nucleus = top_p is not None and 0.0 < top_p < 1.0
+    # row statistics (+ parity export), then the greedy decision or the five-launch stochastic draw
+    _lib.count(1 + int(export_probs) + (1 if greedy else 5 + int(nucleus)))
     return out
 
 

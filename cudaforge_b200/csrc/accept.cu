@@ -592,7 +592,8 @@ struct SeqState {
   float r;     // the draw's uniform
   float sum;   // stage 0 result: exact residual mass
   int vkind;   // stage 1 values: 1 = residual / sum, 2 = target row (mass <= 1e-6)
-  int pad[2];
+  uint32_t tp_key;  // nucleus (top-p) bonus draw: logits with order key >= tp_key are kept
+  float tp_sum;     // ... and their probability mass (0: no nucleus filter)
 };
 
 struct ChunkInfo {
@@ -630,6 +631,12 @@ __device__ __forceinline__ float block_sum256(float v, float *red) {
 //   kind 0: target probabilities of `row`
 //   kind 1: residual max(0, p - q) of `row`
 //   kind 2: residual / sum
+// Order key of a float: unsigned comparison of keys = numeric comparison of values.
+__device__ __forceinline__ uint32_t order_key(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 template <typename T>
 struct ChainVals {
   const T *xt, *xd;
@@ -637,11 +644,17 @@ struct ChainVals {
   float c, sum;
   int64_t V;
   int kind;
+  uint32_t tp_key;
   __device__ __forceinline__ void operator()(int64_t i0, float (&o)[8]) const {
     load8<T>(xt, i0, V, o);
     if (kind == 0) {
 #pragma unroll
       for (int q = 0; q < 8; ++q) o[q] = prob_of(o[q], c, st_t);
+      return;
+    }
+    if (kind == 3) {  // nucleus: kept probabilities / their mass, the rest 0
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] = order_key(o[q]) >= tp_key ? __fdiv_rn(prob_of(o[q], c, st_t), sum) : 0.0f;
       return;
     }
     float d8[8];
@@ -668,6 +681,19 @@ __device__ __forceinline__ ChainVals<T> chain_vals(const cf_accept_args &a, floa
   f.sum = sum;
   f.V = a.vocab;
   f.kind = kind;
+  f.tp_key = 0;
+  return f;
+}
+
+// The chain values of sequence state sq for value kind `kind`.
+template <typename T>
+__device__ __forceinline__ ChainVals<T> chain_vals_of(const cf_accept_args &a, float c, const RowStat *st, int b,
+                                                      const SeqState &sq, int kind) {
+  ChainVals<T> f = chain_vals<T>(a, c, st, b, sq.row, kind == 3 ? 0 : kind, kind == 3 ? sq.tp_sum : sq.sum);
+  if (kind == 3) {
+    f.kind = 3;
+    f.tp_key = sq.tp_key;
+  }
   return f;
 }
 
@@ -721,6 +747,7 @@ prep_kernel(cf_accept_args a, float c, const RowStat *stats, SeqState *seq, Chun
     if (j == 0) {
       SeqState sq{};
       sq.mode = mode; sq.row = row; sq.na = na; sq.r = s_r; sq.sum = 0.0f; sq.vkind = 0;
+      sq.tp_key = 0; sq.tp_sum = 0.0f;
       seq[b] = sq;
       if (mode < 0) { a.out_num_accepted[b] = -1; a.out_eos[b] = 0; }
       if (mode == kDone) { out[na] = a.eos_token_id; a.out_num_accepted[b] = na; a.out_eos[b] = 1; }
@@ -760,7 +787,7 @@ prep_kernel(cf_accept_args a, float c, const RowStat *stats, SeqState *seq, Chun
 __device__ __forceinline__ int chain_kind(const SeqState &sq, int stage, bool &search) {
   search = true;
   if (stage == 0) {
-    if (sq.mode == kBonus) return 0;
+    if (sq.mode == kBonus) return sq.tp_sum > 0.0f ? 3 : 0;
     if (sq.mode == kResidual) { search = false; return 1; }
     return -1;
   }
@@ -799,7 +826,7 @@ maps_kernel(cf_accept_args a, float c, const RowStat *stats, const SeqState *seq
   __syncthreads();
   const int ue = s_ue;
   const RowStat *st = stats + (int64_t)b * (2 * a.k + 1);
-  const ChainVals<T> f = chain_vals<T>(a, c, st, b, sq.row, kind, sq.sum);
+  const ChainVals<T> f = chain_vals_of<T>(a, c, st, b, sq, kind);
   // thread t owns the contiguous elements [lo + t*per, lo + (t+1)*per): maps compose in thread order
   const int64_t per = ((hi - lo + kChainThreads - 1) / kChainThreads + 7) & ~(int64_t)7;
   IncMap m{0, 0};
@@ -830,6 +857,93 @@ maps_kernel(cf_accept_args a, float c, const RowStat *stats, const SeqState *seq
   }
 }
 
+// Nucleus (top-p) filter of the bonus draw, one CTA per sequence in bonus
+// mode.  The reference (speculative.py:58-84) sorts the row, keeps every token
+// whose exclusive cumulative probability in descending order is <= top_p
+// (the token that crosses top_p included) and renormalises.  Here a token x is
+// kept when the probability mass of the logits strictly above it is <= top_p;
+// for distinct logits that is the same set, and tied logits are kept or
+// dropped together (independent of sort stability).  The kept set is
+// {order_key(x) >= k*}, k* the smallest key whose strictly-greater mass is
+// <= top_p, found by bisection over the 32-bit keys with fixed-order sums; the
+// approximate chunk sums of the renormalised values then predict the maps.
+template <typename T>
+__global__ void __launch_bounds__(kScanThreads, 1)
+nucleus_kernel(cf_accept_args a, float c, const RowStat *stats, SeqState *seq, ChunkInfo *ci) {
+  __shared__ float red[kScanThreads / 32];
+  __shared__ float s_tot;
+  const int b = blockIdx.x, tid = threadIdx.x;
+  SeqState sq = seq[b];
+  if (sq.mode != kBonus) return;
+  const int64_t V = a.vocab;
+  const RowStat *st = stats + (int64_t)b * (2 * a.k + 1);
+  const T *x = row_ptr<T>(a.target_logits, a.target_seq_stride, a.target_row_stride, b, sq.row);
+  const RowStat stt = st[a.k + sq.row];
+  // fixed-order mass of the logits whose key is > kgt (strict) or >= kge
+  auto mass = [&](uint32_t k, bool strict) -> float {
+    float m = 0.0f;
+    for (int64_t i0 = (int64_t)tid * 8; i0 < V; i0 += (int64_t)kScanThreads * 8) {
+      float v[8];
+      load8<T>(x, i0, V, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t kk = order_key(v[q]);
+        if (i0 + q < V && (strict ? kk > k : kk >= k)) m += prob_of(v[q], c, stt);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
+    __syncthreads();
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.0f;
+      for (int i = 0; i < kScanThreads / 32; ++i) t += red[i];
+      s_tot = t;
+    }
+    __syncthreads();
+    return s_tot;
+  };
+  // smallest k with mass(> k) <= top_p: the predicate is monotone in k
+  uint32_t lo = 0, hi = 0xffffffffu;
+  if (mass(0u, true) <= a.top_p) hi = 0u;
+  while (lo + 1 < hi) {
+    const uint32_t mid = lo + (hi - lo) / 2;
+    if (mass(mid, true) <= a.top_p) hi = mid;
+    else lo = mid;
+  }
+  const float kept = mass(hi, false);
+  int64_t lo_c, hi_c;
+  if (tid == 0) {
+    sq.tp_key = hi;
+    sq.tp_sum = kept > 0.0f ? kept : 1.0f;
+    seq[b] = sq;
+  }
+  // approximate chunk sums of the renormalised kept values (they predict the maps' grids)
+  const float inv = 1.0f / (kept > 0.0f ? kept : 1.0f);
+  for (int j = 0; j < kNch; ++j) {
+    chunk_range(V, j, lo_c, hi_c);
+    float m = 0.0f;
+    for (int64_t i0 = lo_c + (int64_t)tid * 8; i0 < hi_c; i0 += (int64_t)kScanThreads * 8) {
+      float v[8];
+      load8<T>(x, i0, V, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (i0 + q < hi_c && order_key(v[q]) >= hi) m += prob_of(v[q], c, stt) * inv;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
+    __syncthreads();
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.0f;
+      for (int i = 0; i < kScanThreads / 32; ++i) t += red[i];
+      ci[(int64_t)b * kNch + j].approx[0] = t;
+    }
+  }
+}
+
 template <typename T, int STAGE>
 __global__ void __launch_bounds__(kScanThreads, 1)
 resolve_kernel(cf_accept_args a, float c, const RowStat *stats, SeqState *seq, const ChunkInfo *ci) {
@@ -845,7 +959,7 @@ resolve_kernel(cf_accept_args a, float c, const RowStat *stats, SeqState *seq, c
   if (kind < 0) return;
   const int64_t V = a.vocab;
   const RowStat *st = stats + (int64_t)b * (2 * a.k + 1);
-  const ChainVals<T> f = chain_vals<T>(a, c, st, b, sq.row, kind, sq.sum);
+  const ChainVals<T> f = chain_vals_of<T>(a, c, st, b, sq, kind);
   for (int i = tid; i < kNch; i += kScanThreads) {
     s_ue[i] = ci[(int64_t)b * kNch + i].ue;
     s_me[i] = ci[(int64_t)b * kNch + i].me;
@@ -1091,6 +1205,7 @@ int launch_accept(const cf_accept_args &a, cudaStream_t stream) {
   ChunkInfo *ci = reinterpret_cast<ChunkInfo *>(base + (size_t)a.batch * sizeof(SeqState));
   const dim3 gc(kNch, a.batch);
   prep_kernel<T><<<gc, kChainThreads, 0, stream>>>(a, c, stats, seq, ci);
+  if (a.top_p > 0.0f && a.top_p < 1.0f) nucleus_kernel<T><<<a.batch, kScanThreads, 0, stream>>>(a, c, stats, seq, ci);
   maps_kernel<T, 0><<<gc, kChainThreads, 0, stream>>>(a, c, stats, seq, ci);
   resolve_kernel<T, 0><<<a.batch, kScanThreads, 0, stream>>>(a, c, stats, seq, ci);
   maps_kernel<T, 1><<<gc, kChainThreads, 0, stream>>>(a, c, stats, seq, ci);

@@ -43,12 +43,19 @@ class SpeculativeBatchResult:
 class SpeculativeEngine:
     def __init__(self, draft_runner: Any, target_runner: Any, num_speculative_tokens: int = 5,
                  temperature: float = 1.0, top_p: float = 0.9, eos_token_id: int = -1,
-                 greedy: bool = False, seed: int = 0) -> None:
+                 greedy: bool = False, seed: int = 0, nucleus_bonus: bool = False) -> None:
+        """The reference's constructor (speculative.py:28-50) plus: eos_token_id,
+        greedy verification, the seed of the device uniforms, and
+        nucleus_bonus -- True applies top_p to the bonus draw as the reference
+        Python engine does (speculative.py:188-195); False (default) follows
+        the reference C++ verifier, which ignores top_p (speculative.h:17),
+        so that decisions stay bit-exact with it."""
         self.draft_runner = draft_runner
         self.target_runner = target_runner
         self.k = num_speculative_tokens
         self.temperature = max(temperature, 1e-5)  # speculative.py:50
-        self.top_p = top_p  # kept for API parity; the native verifier ignores it (speculative.h:17)
+        self.top_p = top_p
+        self.nucleus_bonus = nucleus_bonus
         self.eos_token_id = eos_token_id
         self.greedy = greedy
         self.total_draft_tokens = 0
@@ -112,6 +119,8 @@ class SpeculativeEngine:
         B, K = draft_tokens.shape
         if not greedy and uniforms is None:
             uniforms = self._uniforms(B, K + 1, target_logits.device)
+        if self.nucleus_bonus and "top_p" not in kw:
+            kw["top_p"] = self.top_p
         return accept_sample(draft_logits, target_logits, draft_tokens, uniforms, temperature=self.temperature,
                              eos_token_id=self.eos_token_id, greedy=greedy, **kw)
 

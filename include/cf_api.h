@@ -108,6 +108,10 @@ typedef struct cf_accept_args {
   void *workspace;           /* >= cf_accept_workspace_bytes(B, K) bytes, 16-B aligned */
   float *probs_draft;        /* optional parity export                   */
   float *probs_target;       /* optional parity export                   */
+  float top_p;               /* in (0, 1): nucleus filter on the bonus draw (the
+                              * reference Python engine's top-p, speculative.py:58-84,
+                              * :188-195; not in the reference C++ path, so not
+                              * parity-pinned); 0 or >= 1: off */
 } cf_accept_args;
 
 size_t cf_accept_workspace_bytes(int32_t batch, int32_t k);
