@@ -44,12 +44,17 @@ def test_bonus_draw_follows_the_nucleus_rule(top_p):
     for b in range(B):
         keep, q, excl = _nucleus(logits[b, 0].double().numpy(), T, top_p)
         assert keep[tok[b]], b
-        if np.min(np.abs(excl - top_p)) < 1e-4:
-            continue  # a kept-set boundary within float32 rounding of top_p
+        # the token that crosses top_p (last kept in descending order) and the first dropped one
+        ex = np.sort(excl)
+        k = int(np.searchsorted(ex, top_p, side="right"))
+        if abs(ex[k - 1] - top_p) < 1e-5 or (k < len(ex) and abs(ex[k] - top_p) < 1e-5):
+            continue  # the kept set is within float32 rounding of top_p
         cum = np.cumsum(q)
-        want = int(np.searchsorted(cum, float(u[b, 0]), side="left"))
-        if np.min(np.abs(cum - float(u[b, 0]))) < 1e-5:
-            continue  # the uniform sits on a float32 rounding boundary of the CDF
+        r = float(u[b, 0])
+        want = int(np.searchsorted(cum, r, side="left"))
+        lo_edge = cum[want - 1] if want > 0 else 0.0
+        if want < V and (cum[want] - r < 1e-5 or r - lo_edge < 1e-5):
+            continue  # the uniform sits within float32 rounding of a CDF step
         assert tok[b] == want, b
         checked += 1
     assert checked > B // 2
