@@ -949,7 +949,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
 resolve_kernel(cf_accept_args a, float c, const RowStat *stats, SeqState *seq, const ChunkInfo *ci) {
   __shared__ ScanShared sh;
   __shared__ int s_ue[kNch], s_me[kNch], s_mo[kNch];
-  __shared__ float s_buf[kSerial];
+  __shared__ __align__(16) float s_buf[kSerial];
   __shared__ float s_cum;
   __shared__ long long s_hit;
   const int b = blockIdx.x, tid = threadIdx.x;
@@ -979,9 +979,18 @@ resolve_kernel(cf_accept_args a, float c, const RowStat *stats, SeqState *seq, c
   if (tid == 0) {
     float cum = 0.0f;
     long long hit = -1;
-    for (int i = 0; i < n0; ++i) {
-      cum = __fadd_rn(cum, s_buf[i]);
-      if (search && r <= cum) { hit = i; break; }
+    // eight values per pair of 16-byte shared loads, so the dependent adds do not wait on each load
+    for (int i = 0; i < n0 && hit < 0; i += 8) {
+      const float4 x = reinterpret_cast<const float4 *>(s_buf)[i / 4];
+      const float4 y = reinterpret_cast<const float4 *>(s_buf)[i / 4 + 1];
+      const float v[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (i + q < n0 && hit < 0) {
+          cum = __fadd_rn(cum, v[q]);
+          if (search && r <= cum) hit = i + q;
+        }
+      }
     }
     s_cum = cum;
     s_hit = hit;
