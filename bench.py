@@ -608,6 +608,82 @@ def run_reference(args):
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def generate_cfg2(tcfg, dcfg, prompts, K, new_tokens, temperature, greedy, device, seed=0):
+    """speculative generation with the tiny fp16 pair.  Both
+    models prefill the prompts (all but the last token) through the paged
+    runner; then full rounds -- the device-resident K-step draft loop, the
+    verify + accept + commit step, the draft advance -- run until every
+    sequence has `new_tokens` emitted tokens.  Returns (emitted token lists,
+    device ms of the rounds, rounds, the verifier, the models)."""
+    from cudaforge_b200.drafter import BatchDrafter
+    from cudaforge_b200.model import LlamaModel
+    from cudaforge_b200.runner import PagedRunner
+    from cudaforge_b200.verifier import BatchVerifier
+    B, P = prompts.shape
+    ids = list(range(B))
+    bps = math.ceil((P + new_tokens + 2 * (K + 1)) / 16) + 2
+    target = LlamaModel(tcfg, device=device, seed=1000 + seed)
+    draft = LlamaModel(dcfg, device=device, seed=2000 + seed)
+    tcache = target.make_cache(B * bps + 8, max_batch=B, max_blocks_per_seq=bps + 4)
+    dcache = draft.make_cache(B * (bps + 1) + 8, max_batch=B, max_blocks_per_seq=bps + 4)
+    head = prompts[:, :-1].tolist()
+    PagedRunner(target, tcache, ids).prefill(head)
+    PagedRunner(draft, dcache, ids).prefill(head)
+    ver = BatchVerifier(target, tcache, ids, K, temperature=temperature, greedy=greedy,
+                        max_blocks_per_seq=bps + 4, use_graph=True)
+    ver.register_context(head, prompts[:, -1], registered=True)
+    dr = BatchDrafter(draft, dcache, ids, K, temperature=temperature, greedy=greedy, max_blocks_per_seq=bps + 4,
+                      use_graph=True)
+    dr.register_context(head, prompts[:, -1], registered=True)
+    gen = torch.Generator(device=device).manual_seed(77 + seed)
+    out = [[] for _ in range(B)]
+    rounds = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    while min(len(o) for o in out) < new_tokens:
+        ud = None if greedy else torch.rand(B, K, generator=gen, device=device)
+        uv = None if greedy else torch.rand(B, K + 1, generator=gen, device=device)
+        dt, dl = dr.draft(ud)
+        res = ver.step(dt, dl, uv)
+        n = (ver.n_pinned.clamp_min(0) + 1).tolist()
+        toks = res.tokens.cpu().tolist()
+        for b in range(B):
+            out[b].extend(toks[b][: n[b]])
+        dr.advance(res, n)
+        rounds += 1
+    e1.record()
+    torch.cuda.synchronize(device)
+    ver.check_status()
+    return out, e0.elapsed_time(e1), rounds, ver, target
+
+
+def run_cfg2(args):
+    """--config tiny: BASELINE config 2 on one GPU -- the tiny fp16 target /
+    draft pair (random init), B=8, 128-token random prompts, K=4 chain
+    drafting, 128 new tokens per sequence, greedy and at T=0.8.  The metric is
+    whole-job generated tokens per second of the speculative rounds (device
+    time, prefill excluded).  Logits parity for this workload is the GPU test
+    tests/test_cfg2_gpu.py."""
+    from cudaforge_b200.model import TINY_DRAFT, TINY_TARGET
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    B, P, K, N = 8, 128, 4, 128
+    prompts = torch.randint(0, TINY_TARGET.vocab, (B, P), generator=torch.Generator().manual_seed(7))
+    modes = {}
+    for name, greedy, T in (("greedy", True, 1.0), ("t0.8", False, 0.8)):
+        generate_cfg2(TINY_TARGET, TINY_DRAFT, prompts, K, 16, T, greedy, device)  # warm-up (captures graphs)
+        out, ms, rounds, ver, _ = generate_cfg2(TINY_TARGET, TINY_DRAFT, prompts, K, N, T, greedy, device)
+        emitted = sum(len(o) for o in out)
+        modes[name] = {"generated_tok_s": round(emitted / (ms / 1e3), 1), "ms": round(ms, 2), "rounds": rounds,
+                       "tokens_per_round_per_seq": round(emitted / (rounds * B), 3)}
+    return {"metric": "generated tok/s of speculative decoding (cfg2 tiny fp16 pair)",
+            "value": modes["t0.8"]["generated_tok_s"], "unit": UNIT, "n_gpus": 1, "higher_is_better": True,
+            "dtype": "f16", "data": "synthetic: random-init fp16 weights N(0,0.02), random prompt ids",
+            "config": {"workload": "cfg2 tiny pair: target L4/d512/8x64/FFN1408, draft L1/d256/4x64/FFN704, "
+                                   "V 32000, B=8, 128-token prompts, K=4, 128 new tokens", "batch": B, "k": K},
+            "modes": modes}
+
+
 def run_case(args):
     """Single-kernel cases at the bench shapes (for ncu captures and per-shape
     timing); prints one JSON line per shape."""
@@ -697,7 +773,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="8b", choices=["8b", "tiny", "8b-tree", "70b-tp"],
-                    help="8b = cfg3 chain (default); 8b-tree = cfg4 (B=32, 4096 context, 64-node tree); "
+                    help="8b = cfg3 chain (default); tiny = cfg2 generation with the tiny fp16 pair; 8b-tree = cfg4 (B=32, 4096 context, 64-node tree); "
                          "70b-tp = cfg5 (70B tensor-parallel over the ranks, B=128, 2048 context, K=4)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU (weak scaling)")
     ap.add_argument("--global-batch", type=int, default=None,
@@ -724,6 +800,9 @@ def main():
         args.k = 4
     if args.case:
         run_case(args)
+        return
+    if args.config == "tiny" and args.impl == "ours":
+        print(json.dumps(run_cfg2(args)), flush=True)
         return
     if args.impl == "reference":
         out = run_reference(args)

@@ -83,12 +83,15 @@ class BatchVerifier:
     def tables(self) -> torch.Tensor:
         return self.tables_dev
 
-    def register_context(self, prompts, last_tokens) -> None:
+    def register_context(self, prompts, last_tokens, registered: bool = False) -> None:
         """Register each sequence's cached prompt (page tables) and set row 0
         (the last emitted token, not yet cached).  Pool contents come from a
-        prefill or from fill_synthetic_kv()."""
-        for sid, p in zip(self.seq_ids, prompts):
-            self.cache.register_sequence_with_prefix(sid, p)
+        prefill or from fill_synthetic_kv().  registered=True adopts sequences
+        already in the cache with exactly len(prompts[b]) tokens (e.g. after
+        PagedRunner.prefill)."""
+        if not registered:
+            for sid, p in zip(self.seq_ids, prompts):
+                self.cache.register_sequence_with_prefix(sid, p)
         self.ctx_host = [len(p) for p in prompts]
         self.ctx.copy_(torch.tensor(self.ctx_host, dtype=torch.int32))
         self.tokens[:, 0].copy_(torch.as_tensor(last_tokens, dtype=torch.int32))
