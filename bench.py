@@ -148,7 +148,8 @@ def setup(args, rank, device, world=1):
     target = LlamaModel(tcfg, device=device, seed=1000)
     cache = target.make_cache(B * blocks_per_seq + 8, max_batch=B, max_blocks_per_seq=blocks_per_seq + 4)
     ver = BatchVerifier(target, cache, ids, K, temperature=args.temperature,
-                        max_blocks_per_seq=blocks_per_seq + 4, use_graph=not args.no_graph)
+                        max_blocks_per_seq=blocks_per_seq + 4, use_graph=not args.no_graph,
+                        device_tables=not args.host_tables)
     g = torch.Generator().manual_seed(7)
     prompts = torch.randint(0, tcfg.vocab, (B * world, P), generator=g)[ids[0]: ids[-1] + 1]
     ver.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
@@ -286,13 +287,18 @@ def run_ours(args):
     step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     e0.record()
     step_ev[0].record()
+    dev_tab = getattr(ver, "dtab", None) is not None or getattr(getattr(ver, "base", None), "dtab", None) is not None
+    em0 = ver.dtab.emitted if dev_tab else 0
     for i in range(args.steps):
         res = ver.step(dtok, dlog, uni[args.warmup + i])
         step_ev[i + 1].record()
-        tokens_per_step.append(int((ver.n_pinned.clamp_min(0) + 1).sum()))
+        if not dev_tab:  # host tables: the step already synchronised for its counts
+            tokens_per_step.append(int((ver.n_pinned.clamp_min(0) + 1).sum()))
     e1.record()
     barrier()
     ver.check_status()  # a timed-out wait or a bad page id voids the measurement
+    if dev_tab:  # device tables: the host replayed the steps' counts lazily
+        tokens_per_step = [(ver.dtab.emitted - em0) / args.steps] * args.steps
     launches = _lib.LAUNCHES[0] - l0
     ms = e0.elapsed_time(e1)
     step_ms = sorted(step_ev[i].elapsed_time(step_ev[i + 1]) for i in range(args.steps))
@@ -303,6 +309,8 @@ def run_ours(args):
     kp = max(2, min(args.steps, 4))
     ctx_sums = []
     for i in range(kp):
+        if hasattr(ver, "sync"):
+            ver.sync()
         ctx_sums.append(sum(ver.ctx_host))  # context of the step's attention (before its commit)
         torch.cuda._sleep(60_000_000)  # ~30 ms of device time at 1.9 GHz
         ver.step(dtok, dlog, uni[total_steps + i], timer=kt)
@@ -347,7 +355,7 @@ def run_ours(args):
         for i in range(2):  # the drafter captures its graph on its second round
             dt_, dl_ = drafter.draft(ud[i])
             r = ver.step(dt_, dl_, uni[i])
-            drafter.advance(r, (ver.n_pinned.clamp_min(0) + 1).tolist())
+            drafter.advance(r, (r.num_accepted.clamp_min(0) + 1).tolist())
         barrier()
         d_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
         r0 = torch.cuda.Event(enable_timing=True)
@@ -359,7 +367,7 @@ def run_ours(args):
             dt_, dl_ = drafter.draft(ud[2 + i])
             d_ev[i][1].record()
             r = ver.step(dt_, dl_, uni[i])
-            n_host = (ver.n_pinned.clamp_min(0) + 1).tolist()
+            n_host = (r.num_accepted.clamp_min(0) + 1).tolist()  # the draft tables grow on the host
             round_tokens += sum(n_host)
             drafter.advance(r, n_host)
         r1.record()
@@ -453,6 +461,8 @@ def run_ours(args):
                                        + ("fixed global batch split over the ranks" if args.global_batch
                                           else "fixed batch per GPU") + ")"),
                        "l2": "inputs larger than L2 (GB-sized INT4 weights + KV pools per GPU)",
+                       "page_tables": "host (round trip per step)" if args.host_tables or tp or tree
+                                      else "device-resident (one CUDA graph per step)",
                        "mean_accepted_per_seq_step": round(tok_all / (args.steps * B * (1 if tp else world)) - 1, 3)},
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
@@ -784,6 +794,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every kernel eagerly (no CUDA graphs)")
     ap.add_argument("--no-rounds", action="store_true", help="skip the full-round (draft loop) timing")
+    ap.add_argument("--host-tables", action="store_true",
+                    help="grow the page tables on the host every step (a round trip per step) instead of on the device")
     ap.add_argument("--case", default=None, choices=["gemm", "attention", "accept"],
                     help="time a single kernel at the bench shapes (profiling aid)")
     ap.add_argument("--shape", default=None, help="NxK for --case gemm")

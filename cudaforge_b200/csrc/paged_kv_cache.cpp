@@ -298,6 +298,15 @@ extern "C" int cf_kvcache_prepare_batch(cf_kvcache *h, const uint64_t *seqs, uin
   return CF_OK;
 }
 
+extern "C" int cf_kvcache_export_free_stack(cf_kvcache *h, int32_t *out, uint32_t cap, uint32_t *n) {
+  if (!h || !n) return CF_EINVAL;
+  Cache &c = h->c;
+  std::lock_guard<std::mutex> g(c.mu);
+  *n = (uint32_t)c.free_stack.size();
+  if (out) std::memcpy(out, c.free_stack.data(), (c.free_stack.size() < cap ? c.free_stack.size() : cap) * 4);
+  return CF_OK;
+}
+
 extern "C" int cf_kvcache_get_stats(cf_kvcache *h, cf_kv_stats *s) {
   if (!h || !s) return CF_EINVAL;
   Cache &c = h->c;

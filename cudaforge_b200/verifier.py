@@ -34,7 +34,11 @@ from .model import LlamaModel
 class BatchVerifier:
     def __init__(self, model: LlamaModel, cache, seq_ids: Sequence[int], k: int, *, temperature: float = 1.0,
                  greedy: bool = False, eos_token_id: int = -1, max_blocks_per_seq: int = 512,
-                 use_graph: bool = False):
+                 use_graph: bool = False, device_tables: bool = False):
+        """device_tables=True keeps the page tables on the device (DeviceTables):
+        the page-table growth runs as a kernel inside the step, the whole step
+        is one CUDA graph in graph mode and the host never waits for it; the
+        host cache and ctx_host catch up lazily (sync() / check_status())."""
         self.model, self.cache = model, cache
         self.seq_ids = list(seq_ids)
         self.B, self.K, self.R = len(self.seq_ids), k, k + 1
@@ -69,6 +73,8 @@ class BatchVerifier:
         self.start = torch.zeros(B, dtype=torch.int32, device=dev)
         self.kernels_per_step = 0
         self._keep = []
+        self.device_tables = device_tables
+        self.dtab = None
 
     # ---- state ----
     def _upload_tables(self, stream=None):
@@ -81,7 +87,7 @@ class BatchVerifier:
         self.tables_dev.copy_(self.tables_fixed, non_blocking=True)
 
     def tables(self) -> torch.Tensor:
-        return self.tables_dev
+        return self.dtab.tables if self.dtab is not None else self.tables_dev
 
     def register_context(self, prompts, last_tokens, registered: bool = False) -> None:
         """Register each sequence's cached prompt (page tables) and set row 0
@@ -96,6 +102,11 @@ class BatchVerifier:
         self.ctx.copy_(torch.tensor(self.ctx_host, dtype=torch.int32))
         self.tokens[:, 0].copy_(torch.as_tensor(last_tokens, dtype=torch.int32))
         self._upload_tables()
+        if self.device_tables:
+            from .device_tables import DeviceTables
+            self.dtab = DeviceTables(self.cache, self.seq_ids, self.cap, self.model.device)
+            self.dtab.upload(self.ctx)
+
 
     def fill_synthetic_kv(self, gen: torch.Generator, std: float = 1.0) -> None:
         """Seeded random K/V for every pool slot (stands in for a prefill of
@@ -127,6 +138,8 @@ class BatchVerifier:
         bf = self.model.buffers(B, R)
         self.start.copy_(self.ctx)
         with (timer or _null_timer)("commit"):
+            if self.dtab is not None:  # the page tables grow on the device first
+                self.dtab.append(res.num_accepted, self.ctx, 1, status=self.status)
             ops.kv_commit(self.cache, bf["k_new"], bf["v_new"], res.num_accepted, self.start, self.tables(),
                           n_commit_add=1, status=self.status)
         # next round: context grows by n, row 0 = the final token
@@ -140,12 +153,19 @@ class BatchVerifier:
         g_uni = None if uniforms is None else uniforms.clone()
         self.g_in = (g_tok, draft_logits, g_uni)  # draft logits are captured by address
         max_ctx = self.cap * self.cache.get_config().block_size
-        g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g1):
-            self._forward_accept(g_tok, draft_logits, g_uni, max_context=max_ctx)
-        with torch.cuda.graph(g2):
-            self._commit_update(self.res)
-        self.graphs = (g1, g2)
+        if self.dtab is not None:  # the whole step, page-table growth included, is one graph
+            g1 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g1):
+                self._forward_accept(g_tok, draft_logits, g_uni, max_context=max_ctx)
+                self._commit_update(self.res)
+            self.graphs = (g1, None)
+        else:
+            g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g1):
+                self._forward_accept(g_tok, draft_logits, g_uni, max_context=max_ctx)
+            with torch.cuda.graph(g2):
+                self._commit_update(self.res)
+            self.graphs = (g1, g2)
         # hold every workspace the captured kernels address: the capture plans for
         # max_context, which can grow a cached workspace inside the capture, and a
         # later call may replace the cache entry while this graph still uses it
@@ -174,8 +194,13 @@ class BatchVerifier:
                 g_dlog.copy_(draft_logits)
             self.graphs[0].replay()
             res = self.res
+        elif self.dtab is not None:
+            max_ctx = self.cap * self.cache.get_config().block_size
+            res = self._forward_accept(draft_tokens, draft_logits, uniforms, timer=timer, max_context=max_ctx)
         else:
             res = self._forward_accept(draft_tokens, draft_logits, uniforms, timer=timer)
+        if self.dtab is not None:
+            return self._finish_device_step(res, graph, timer, l0)
         self.n_pinned.copy_(res.num_accepted, non_blocking=True)
         self.st.snapshot()
         torch.cuda.current_stream(self.model.device).synchronize()
@@ -194,7 +219,40 @@ class BatchVerifier:
         self.ctx_host = [c + x for c, x in zip(self.ctx_host, n)]
         return res
 
+    def _finish_device_step(self, res, graph, timer, l0) -> AcceptResult:
+        from . import _lib
+        if graph and self.graphs is not None:
+            _lib.count(self.kernels_per_step)
+        else:
+            self._commit_update(res, timer=timer)
+            if not self.kernels_per_step:
+                self.kernels_per_step = _lib.LAUNCHES[0] - l0
+        # host bookkeeping trails the device: queue this step's counts, replay finished steps
+        self.dtab.record(res.num_accepted, 1)
+        self._catch_up(False)
+        # errors of earlier steps surface here (the status copy lands asynchronously)
+        self.st.check("BatchVerifier.step")
+        self.st.snapshot()
+        return res
+
+    def _catch_up(self, block: bool) -> None:
+        if self.dtab.catch_up(block_all=block):
+            self.ctx_host = self._host_ctx()  # the host cache now holds every replayed step
+
+    def _host_ctx(self):
+        tables = torch.zeros(self.B * self.cap, dtype=torch.int32)
+        ctx = torch.zeros(self.B, dtype=torch.int32)
+        self.cache.prepare_batch_into(self.seq_ids, tables, ctx)
+        return ctx.tolist()
+
+    def sync(self) -> None:
+        """Device-table mode: wait for every queued step and bring the host
+        cache (page tables, ctx_host) up to date."""
+        if self.dtab is not None:
+            self._catch_up(True)
+
     def check_status(self) -> None:
         """Synchronise and raise DeviceError if a kernel since the last check
         (e.g. the last step's KV commit) recorded an error."""
+        self.sync()
         self.st.sync_check("BatchVerifier")

@@ -314,6 +314,11 @@ int cf_kvcache_prepare_batch(cf_kvcache *h, const uint64_t *seqs, uint32_t batch
                              uint32_t table_cap, int32_t *context_lens, uint32_t *max_blocks_out);
 /* get_stats (:423-445) */
 int cf_kvcache_get_stats(cf_kvcache *h, cf_kv_stats *s);
+/* The free stack, bottom to top (the next block handed out is out[n - 1]),
+ * for a device-resident copy (cf_kv_append_device).  *n = its size; at most
+ * cap entries are written.  No reference counterpart (the reference's stack
+ * is private, paged_kv_cache.cpp:44-53). */
+int cf_kvcache_export_free_stack(cf_kvcache *h, int32_t *out, uint32_t cap, uint32_t *n);
 /* get_key_block_ptr / get_value_block_ptr (:409-421) */
 void *cf_kvcache_key_block_ptr(cf_kvcache *h, int32_t block, uint32_t layer);
 void *cf_kvcache_value_block_ptr(cf_kvcache *h, int32_t block, uint32_t layer);
@@ -410,6 +415,36 @@ typedef struct cf_kv_commit_args {
 } cf_kv_commit_args;
 
 int cf_kv_commit(const cf_kv_commit_args *args, void *stream);
+
+/* ---------------------------------------------------------------------------
+ * Device-resident page-table growth: PagedKVCache::append_tokens
+ * (csrc/src/memory/paged_kv_cache.cpp:255-286) for a batch, in batch order,
+ * on the GPU (one launch, graph-capturable, no host round trip).  Sequence b
+ * grows by max(n_append[b], 0) + n_add tokens; context_lens[b] is its length
+ * before the growth, table_len[b] its number of blocks (updated), tables its
+ * fixed-width row [batch][max_blocks] (new blocks appended), free_stack /
+ * *free_top a device copy of the cache's free stack (cf_kvcache_export_free_stack;
+ * blocks are popped from the top, as the host cache pops them).  Identical
+ * tables to cf_kvcache_append_batch when no eviction is needed; when the stack
+ * runs short or a row would exceed max_blocks nothing changes and *status
+ * records CF_ENOMEM / CF_ERANGE.  The host cache is brought up to date by
+ * cf_kvcache_append_batch with the same counts (same result).
+ * ------------------------------------------------------------------------- */
+typedef struct cf_kv_append_args {
+  int32_t batch;
+  int32_t block_size;
+  const int32_t *n_append;    /* [batch] (device; negative counts as 0) */
+  int32_t n_add;              /* added to every count (1: num_accepted + 1) */
+  const int32_t *context_lens;/* [batch] tokens before the growth (device) */
+  int32_t *table_len;         /* [batch] blocks per row (device, updated) */
+  int32_t *tables;            /* [batch][max_blocks] (device, -1 past table_len) */
+  int32_t max_blocks;
+  int32_t *free_stack;        /* device copy, bottom to top */
+  int32_t *free_top;          /* [1] entries in use (device, updated) */
+  int32_t *status;            /* optional status word */
+} cf_kv_append_args;
+
+int cf_kv_append_device(const cf_kv_append_args *args, void *stream);
 
 /* ------------------------------------------------------------------------
  * Fused elementwise pieces of the verify forward (bf16 or fp16 `dtype`).
