@@ -287,7 +287,9 @@ def run_ours(args):
     step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     e0.record()
     step_ev[0].record()
-    dev_tab = getattr(ver, "dtab", None) is not None or getattr(getattr(ver, "base", None), "dtab", None) is not None
+    dev_tab = getattr(ver, "dtab", None) is not None
+    if dev_tab:
+        ver.sync()  # the warm-up steps' counts are replayed before the timed region starts
     em0 = ver.dtab.emitted if dev_tab else 0
     for i in range(args.steps):
         res = ver.step(dtok, dlog, uni[args.warmup + i])
