@@ -281,16 +281,16 @@ def run_ours(args):
     time.sleep(0.5)  # nvidia-smi's first sample takes a moment; the samples span every timed loop below
     tokens_per_step = []
     l0 = _lib.LAUNCHES[0]
+    dev_tab = getattr(ver, "dtab", None) is not None
+    if dev_tab:
+        ver.sync()  # the warm-up steps' counts are replayed on the host before the timed region starts
+    em0 = ver.dtab.emitted if dev_tab else 0
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     e0.record()
     step_ev[0].record()
-    dev_tab = getattr(ver, "dtab", None) is not None
-    if dev_tab:
-        ver.sync()  # the warm-up steps' counts are replayed before the timed region starts
-    em0 = ver.dtab.emitted if dev_tab else 0
     for i in range(args.steps):
         res = ver.step(dtok, dlog, uni[args.warmup + i])
         step_ev[i + 1].record()
