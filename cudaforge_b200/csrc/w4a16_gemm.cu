@@ -222,19 +222,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       issued_x = i + 1;
     }
   } else if (warp == 1) {
-    // ---------------- MMA issue: the whole warp walks the loop, one elected lane issues ----------------
-    const uint32_t idesc = p.idesc;
-    for (int i = 0; i < nkb; ++i) {
-      const int sa = i % SA, sx = i % SX;
-      if (lane == 0) CF_TRACE(6, i);
-      if (!mbar_wait_warp(&afull[sa], (uint32_t)(i / SA) & 1u, p.timeout_ns)) { ok = false; break; }
-      if (lane == 0) CF_TRACE(7, i);
-      if (!mbar_wait_warp(&xfull[sx], (uint32_t)(i / SX) & 1u, p.timeout_ns)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t a_base = smem_u32(a_ring + sa * kAStageBytes);
-      const uint32_t x_base = smem_u32(x_ring + sx * p.x_bytes);
-      if (elect_one()) {
+    // ---------------- MMA issue: one thread; ring slots and phases advance by increments ----------------
+    if (lane == 0) {
+      const uint32_t idesc = p.idesc;
+      int sa = 0, sx = 0;
+      uint32_t pa = 0, px = 0;
+      for (int i = 0; i < nkb; ++i) {
+        CF_TRACE(6, i);
+        if (!mbar_wait(&afull[sa], pa, p.timeout_ns)) { ok = false; break; }
+        CF_TRACE(7, i);
+        if (!mbar_wait(&xfull[sx], px, p.timeout_ns)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(a_ring + sa * kAStageBytes);
+        const uint32_t x_base = smem_u32(x_ring + sx * p.x_bytes);
         CF_TRACE(3, i);
+#pragma unroll
         for (int k16 = 0; k16 < BK / 16; ++k16) {
           const uint64_t bd = desc_kmajor_sw128(x_base + k16 * 32);
           for (int h = 0; h < halves; ++h) {
@@ -251,11 +253,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         mma_commit(&aempty[sa]);
         mma_commit(&xempty[sx]);
         CF_TRACE(8, i);
+        if (++sa == SA) { sa = 0; pa ^= 1u; }
+        if (++sx == SX) { sx = 0; px ^= 1u; }
       }
-      __syncwarp();
+      mma_commit(accf);  // completes when every issued MMA has finished
     }
-    if (elect_one()) mma_commit(accf);  // completes when every issued MMA has finished
     __syncwarp();
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
   } else {
     // ---------------- dequantisation (warps 2-9) straight into TMEM ----------------
     // Warp w may only touch TMEM lanes 32*(w%4)..+31, so warp w owns rows
