@@ -696,9 +696,78 @@ def run_cfg2(args):
             "modes": modes}
 
 
+def _reference_kernel_module(name: str):
+    """A Triton kernel module of the reference, from its offline install under
+    baseline/_ref (the package's __init__ needs the reference's C++ extension,
+    which is not built, so the module file is loaded by itself)."""
+    import importlib.util
+    path = os.path.join(ROOT, "baseline", "_ref", "cudaforge", "kernels", name + ".py")
+    if not os.path.exists(path):
+        raise RuntimeError(f"reference kernels not installed under baseline/_ref ({path})")
+    spec = importlib.util.spec_from_file_location("cf_reference_" + name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _time_us(fn, iters):
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters * 1e3
+
+
+def run_case_reference(args):
+    """--case gemm|attention --impl reference: the reference's own GPU kernels
+    (csrc/kernels/triton/int4_dequant_triton.py:80-131, flash_attn_triton.py:112-172)
+    at the bench shapes, for a kernel-level comparison.  The INT4 kernel takes fp16
+    activations (its tl.dot operand type) and its [K/8, N] packing; the attention
+    kernel is self-attention over [B, H, S, D] with H_q = H_kv, so the verify shape
+    (R query rows against a ctx-long cache) is run as causal self-attention over the
+    ctx + R tokens -- more work than the verify step needs, which is all it can express."""
+    from cudaforge_b200.model import LLAMA_8B
+    dev = torch.device("cuda", 0)
+    c = LLAMA_8B
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.case == "gemm":
+        mod = _reference_kernel_module("int4_dequant_triton")
+        M = args.batch * (args.k + 1)
+        shapes = [(n, k) for _, n, k in c.linear_shapes()] + [(c.vocab, c.d_model)]
+        x = (torch.randn(M, 14336, generator=g, device=dev) * 0.5).to(torch.float16)
+        for n, k in shapes:
+            wq = torch.randint(-2**31, 2**31 - 1, (k // 8, n), generator=g, device=dev, dtype=torch.int32)
+            sc = (torch.randn(k // 128, n, generator=g, device=dev).abs() * 0.002).half()
+            xs = x[:, :k].contiguous()
+            us = _time_us(lambda: mod.int4_gemm_dequant_triton(xs, wq, sc), args.iters)
+            print(json.dumps({"case": "int4_gemm_dequant_triton (reference)", "M": M, "N": n, "K": k,
+                              "us": round(us, 1), "tflops": round(2 * M * n * k / us / 1e6, 1)}), flush=True)
+    elif args.case == "attention":
+        mod = _reference_kernel_module("flash_attn_triton")
+        B, R, P = args.batch, args.k + 1, args.ctx
+        S = P + R
+        q = torch.randn(B, c.n_heads, S, c.head_dim, generator=g, device=dev).to(torch.float16)
+        kk = torch.randn_like(q)
+        vv = torch.randn_like(q)
+        us = _time_us(lambda: mod.flash_attn_triton(q, kk, vv, causal=True), args.iters)
+        print(json.dumps({"case": "flash_attn_triton (reference, causal self-attention)", "B": B, "H": c.n_heads,
+                          "S": S, "us": round(us, 1),
+                          "kv_bytes_of_the_verify_step": B * S * c.n_kv_heads * c.head_dim * 2 * 2}), flush=True)
+    else:
+        raise ValueError("--impl reference supports --case gemm and --case attention")
+
+
 def run_case(args):
     """Single-kernel cases at the bench shapes (for ncu captures and per-shape
     timing); prints one JSON line per shape."""
+    if args.impl == "reference":
+        run_case_reference(args)
+        return
     from cudaforge_b200 import ops
     from cudaforge_b200.gemm import w4a16_gemm
     from cudaforge_b200.model import LLAMA_8B
