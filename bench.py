@@ -186,7 +186,7 @@ def setup_tp(args, rank, world, device):
     target = LlamaModel(tcfg, device=device, seed=1000, tp=TensorParallel(rank, world))
     cache = target.make_cache(B * blocks_per_seq + 8, max_batch=B, max_blocks_per_seq=blocks_per_seq + 4)
     ver = BatchVerifier(target, cache, list(range(B)), K, temperature=args.temperature,
-                        max_blocks_per_seq=blocks_per_seq + 4)
+                        max_blocks_per_seq=blocks_per_seq + 4, micro_batches=args.tp_microbatches)
     g = torch.Generator().manual_seed(7)
     prompts = torch.randint(0, tcfg.vocab, (B, P), generator=g)
     ver.register_context(prompts[:, :-1].tolist(), prompts[:, -1])
@@ -458,7 +458,8 @@ def run_ours(args):
                        "batch_per_gpu": B, "seq_len": args.ctx, **({"tree_nodes": K} if tree else {"k": K}),
                        "temperature": args.temperature,
                        "parallelism": (f"tensor-parallel tp{world} (NCCL all-reduce after O and down, "
-                                       "all-gather of the vocabulary shards)" if tp
+                                       "all-gather of the vocabulary shards; "
+                                       f"{args.tp_microbatches} micro-batch(es) on separate streams)" if tp
                                        else f"batch-sharded dp{world} (no collective; "
                                        + ("fixed global batch split over the ranks" if args.global_batch
                                           else "fixed batch per GPU") + ")"),
@@ -865,6 +866,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch every kernel eagerly (no CUDA graphs)")
     ap.add_argument("--no-rounds", action="store_true", help="skip the full-round (draft loop) timing")
+    ap.add_argument("--tp-microbatches", type=int, default=2, choices=[1, 2],
+                    help="70b-tp: run the batch as two halves on two streams so one half's all-reduces overlap "
+                         "the other's kernels (1 = one batch, collectives in line)")
     ap.add_argument("--host-tables", action="store_true",
                     help="grow the page tables on the host every step (a round trip per step) instead of on the device")
     ap.add_argument("--case", default=None, choices=["gemm", "attention", "accept"],

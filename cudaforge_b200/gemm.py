@@ -53,15 +53,17 @@ MAX_FUSED_SPLITS = 4
 
 
 class _Ws:
-    """Per-device cached split-K workspace (grown on demand)."""
+    """Cached split-K workspace per (device, stream), grown on demand: work on
+    different streams may run concurrently and must not share partials."""
     bufs: dict = {}
 
     @classmethod
-    def get(cls, dev, nbytes):
-        b = cls.bufs.get(dev)
+    def get(cls, dev, nbytes, stream=None):
+        key = (dev, (stream or torch.cuda.current_stream(dev)).cuda_stream)
+        b = cls.bufs.get(key)
         if b is None or b.numel() < nbytes:
             b = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
-            cls.bufs[dev] = b
+            cls.bufs[key] = b
         return b
 
 
@@ -83,7 +85,7 @@ def _gemm(fn, x, w, scales, n, residual, out, split_k, workspace, status, int4, 
     if workspace is not None and workspace.dtype != torch.uint8:
         raise ValueError("workspace must be a uint8 (byte) tensor")
     if need and (workspace is None or workspace.numel() < need):
-        workspace = _Ws.get(x.device, need)
+        workspace = _Ws.get(x.device, need, stream)
     a = _lib.CfGemmArgs(m=M, n=n, k=K, act_dtype=_DT[x.dtype], x=x.data_ptr(), ldx=x.stride(0),
                         w=w.data_ptr(), scales=scales.data_ptr() if scales is not None else None,
                         y=out.data_ptr(), ldy=out.stride(0),
@@ -110,7 +112,7 @@ def w4a16_gemm(x: torch.Tensor, wq_kernel: torch.Tensor, scales: torch.Tensor, *
     and return (fp32 partials [splits, M, N] in the workspace, splits) for an ops.splitk_*
     consumer (residual and out untouched); otherwise y as usual.  Without a caller
     workspace the partials live in a per-device buffer shared by every GEMM: they are
-    valid only until the next GEMM call on that device is enqueued."""
+    valid only until the next GEMM call on that device and stream is enqueued."""
     n = wq_kernel.shape[1]
     L = _lib.lib()
     return _gemm(L.cf_w4a16_gemm, x, wq_kernel, scales, n, residual, out, split_k, workspace, status,

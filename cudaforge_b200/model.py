@@ -226,13 +226,15 @@ class LlamaModel:
         pad = ((cols.numel() + 127) // 128) * 128 if name == "lm_head" else 0
         return lin.take_columns(cols, pad_to=pad)
 
-    def _all_reduce(self, x: torch.Tensor) -> None:
+    def _all_reduce(self, x: torch.Tensor, group=None) -> None:
         import torch.distributed as dist
-        dist.all_reduce(x, group=self.tp.group)
+        dist.all_reduce(x, group=group if group is not None else self.tp.group)
 
     # ---- scratch buffers, sized once per (B, R) and reused (graph friendly) ----
-    def buffers(self, B: int, R: int):
-        key = (B, R)
+    def buffers(self, B: int, R: int, tag: int = 0):
+        """`tag` keeps separate buffer sets for work of the same shape that runs
+        concurrently (micro-batches on two streams)."""
+        key = (B, R) if tag == 0 else (B, R, tag)
         if key not in self._bufs:
             c, M, dev, dt = self.lcfg, B * R, self.device, self.cfg.dtype
             self._bufs[key] = {
@@ -254,17 +256,20 @@ class LlamaModel:
 
     def forward_rows(self, cache, tokens: torch.Tensor, positions: torch.Tensor, block_tables: torch.Tensor,
                      context_lens: torch.Tensor, max_context: int, tree_mask: Optional[torch.Tensor] = None,
-                     status: Optional[torch.Tensor] = None, timer=None) -> torch.Tensor:
+                     status: Optional[torch.Tensor] = None, timer=None, bufs_tag: int = 0,
+                     group=None) -> torch.Tensor:
         """tokens [B, R] int32 (row 0 = last emitted token, then drafts / tree
         nodes), positions [B*R] int32, block tables / context lengths from the
         cache (context = tokens already in the pool).  Returns logits [B*R, V]
         (a reused buffer) and leaves this step's K/V rows in buffers()["k_new"/"v_new"].
+        bufs_tag selects the buffer set (buffers(B, R, bufs_tag)); group overrides the
+        tensor-parallel process group of the collectives (one per concurrent stream).
         `timer(kind)` (optional) returns a context manager wrapped around each
         launch group ("gemm", "attn", "other") for per-kernel timing."""
         c = self.lcfg
         tp = self.tp
         B, R = tokens.shape
-        bf = self.buffers(B, R)
+        bf = self.buffers(B, R, bufs_tag)
         h, xn, qkv, attn, gu, act = bf["h"], bf["xn"], bf["qkv"], bf["attn"], bf["gu"], bf["act"]
         T = timer or _null_timer
         # Split-K GEMMs hand their fp32 partials to the next op, which forms the GEMM output
@@ -299,7 +304,7 @@ class LlamaModel:
                                status=status)
             if tp is not None:
                 with T("comm"):
-                    self._all_reduce(h)
+                    self._all_reduce(h, group)
             with T("other"):
                 if split(r):
                     ops.splitk_rmsnorm(r, lay["ffn_norm"], y=h, out=xn, residual=h, eps=c.eps)
@@ -317,7 +322,7 @@ class LlamaModel:
                                   status=status)
             if tp is not None:
                 with T("comm"):
-                    self._all_reduce(h)
+                    self._all_reduce(h, group)
             pending = r if split(r) else None
         with T("other"):
             if pending is not None:
@@ -332,7 +337,8 @@ class LlamaModel:
         with T("gemm"):
             self.lm_head(xn, out=bf["logits_local"], status=status)
         with T("comm"):
-            dist.all_gather_into_tensor(bf["logits_gather"], bf["logits_local"], group=tp.group)
+            dist.all_gather_into_tensor(bf["logits_gather"], bf["logits_local"],
+                                        group=group if group is not None else tp.group)
             v = c.vocab  # this rank's true vocabulary slice (the shard is padded to 128 columns)
             bf["logits"].view(-1, tp.size, v).copy_(bf["logits_gather"][:, :, :v].permute(1, 0, 2))
         return bf["logits"]

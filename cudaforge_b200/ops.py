@@ -29,14 +29,17 @@ def kv_layout(cache) -> _lib.CfKvLayout:
 
 
 class _Ws:
+    """Cached workspaces per (purpose, device, stream): work on different
+    streams may run concurrently."""
     bufs: dict = {}
 
     @classmethod
-    def get(cls, key, dev, nbytes):
-        b = cls.bufs.get((key, dev))
+    def get(cls, key, dev, nbytes, stream=None):
+        k = (key, dev, (stream or torch.cuda.current_stream(dev)).cuda_stream)
+        b = cls.bufs.get(k)
         if b is None or b.numel() < nbytes:
             b = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=dev)
-            cls.bufs[(key, dev)] = b
+            cls.bufs[k] = b
         return b
 
 
@@ -64,7 +67,7 @@ def verify_attention(cache, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_
     L = _lib.lib()
     need = L.cf_attention_workspace_bytes(ctypes.byref(a))
     if need:
-        ws = _Ws.get("attn", q.device, need)
+        ws = _Ws.get("attn", q.device, need, stream)
         a.workspace, a.workspace_bytes = ws.data_ptr(), need
     _lib.check(L.cf_verify_attention(ctypes.byref(a), _s(stream, q.device)), "cf_verify_attention")
     _lib.count(2 if need else 1)

@@ -34,11 +34,15 @@ from .model import LlamaModel
 class BatchVerifier:
     def __init__(self, model: LlamaModel, cache, seq_ids: Sequence[int], k: int, *, temperature: float = 1.0,
                  greedy: bool = False, eos_token_id: int = -1, max_blocks_per_seq: int = 512,
-                 use_graph: bool = False, device_tables: bool = False):
+                 use_graph: bool = False, device_tables: bool = False, micro_batches: int = 1):
         """device_tables=True keeps the page tables on the device (DeviceTables):
         the page-table growth runs as a kernel inside the step, the whole step
         is one CUDA graph in graph mode and the host never waits for it; the
-        host cache and ctx_host catch up lazily (sync() / check_status())."""
+        host cache and ctx_host catch up lazily (sync() / check_status()).
+        micro_batches=2 (tensor-parallel models, even batch): the two halves of the
+        batch run on two CUDA streams with one process group each, so one half's
+        all-reduces overlap the other half's kernels; acceptance and commit run
+        per half (the same per-sequence results)."""
         self.model, self.cache = model, cache
         self.seq_ids = list(seq_ids)
         self.B, self.K, self.R = len(self.seq_ids), k, k + 1
@@ -75,6 +79,17 @@ class BatchVerifier:
         self._keep = []
         self.device_tables = device_tables
         self.dtab = None
+        self.mb = 1
+        if micro_batches == 2 and getattr(model, "tp", None) is not None and B % 2 == 0:
+            import torch.distributed as dist
+            self.mb = 2
+            # one communicator per stream: collectives of the two halves never share an NCCL queue
+            self.groups = [dist.new_group(backend="nccl"), dist.new_group(backend="nccl")]
+            self.side = torch.cuda.Stream(device=dev)
+            self.ws_mb = [torch.empty(_l.lib().cf_accept_workspace_bytes(B // 2, k) + 256, dtype=torch.uint8,
+                                      device=dev) for _ in range(2)]
+            for t in (0, 1):
+                model.buffers(B // 2, R, tag=t + 1)
 
     # ---- state ----
     def _upload_tables(self, stream=None):
@@ -119,7 +134,42 @@ class BatchVerifier:
                 seg.copy_((torch.randn(seg.numel(), generator=gen, device=seg.device) * std).to(seg.dtype))
 
     # ---- the step ----
+    def _halves(self):
+        h = self.B // 2
+        return [slice(0, h), slice(h, self.B)]
+
+    def _forward_accept_mb(self, draft_tokens, draft_logits, uniforms, timer, max_context) -> AcceptResult:
+        """Two micro-batches; concurrently on two streams unless a timer wants
+        per-kernel events (then one after the other on the current stream)."""
+        from .model import _null_timer
+        B, R, Bm = self.B, self.R, self.B // 2
+        main = torch.cuda.current_stream(self.model.device)
+        self.tokens[:, 1:].copy_(draft_tokens)
+        torch.add(self.ctx.view(B, 1), self.ar, out=self.pos.view(B, R))
+        concurrent = timer is None
+        if concurrent:
+            self.side.wait_stream(main)
+        mctx = max_context if max_context is not None else max(self.ctx_host)
+        for i, sl in enumerate(self._halves()):
+            st = self.side if (concurrent and i == 1) else main
+            with torch.cuda.stream(st):
+                lg = self.model.forward_rows(self.cache, self.tokens[sl], self.pos[sl.start * R: sl.stop * R],
+                                             self.tables()[sl], self.ctx[sl], mctx, status=self.status, timer=timer,
+                                             bufs_tag=i + 1, group=self.groups[i])
+                part = AcceptResult(tokens=self.res.tokens[sl], num_accepted=self.res.num_accepted[sl],
+                                    eos=self.res.eos[sl])
+                with (timer or _null_timer)("accept"):
+                    accept_sample(None if draft_logits is None else draft_logits[sl], lg.view(Bm, R, -1),
+                                  draft_tokens[sl], None if uniforms is None else uniforms[sl],
+                                  temperature=self.temperature, eos_token_id=self.eos, greedy=self.greedy,
+                                  workspace=self.ws_mb[i], out=part)
+        if concurrent:
+            main.wait_stream(self.side)
+        return self.res
+
     def _forward_accept(self, draft_tokens, draft_logits, uniforms, timer=None, max_context=None) -> AcceptResult:
+        if self.mb == 2:
+            return self._forward_accept_mb(draft_tokens, draft_logits, uniforms, timer, max_context)
         B, R = self.B, self.R
         self.tokens[:, 1:].copy_(draft_tokens)
         torch.add(self.ctx.view(B, 1), self.ar, out=self.pos.view(B, R))
@@ -140,8 +190,14 @@ class BatchVerifier:
         with (timer or _null_timer)("commit"):
             if self.dtab is not None:  # the page tables grow on the device first
                 self.dtab.append(res.num_accepted, self.ctx, 1, status=self.status)
-            ops.kv_commit(self.cache, bf["k_new"], bf["v_new"], res.num_accepted, self.start, self.tables(),
-                          n_commit_add=1, status=self.status)
+            if self.mb == 2:  # each half's K/V rows are in its own buffer set
+                for i, sl in enumerate(self._halves()):
+                    bfi = self.model.buffers(self.B // 2, R, tag=i + 1)
+                    ops.kv_commit(self.cache, bfi["k_new"], bfi["v_new"], res.num_accepted[sl], self.start[sl],
+                                  self.tables()[sl], n_commit_add=1, status=self.status)
+            else:
+                ops.kv_commit(self.cache, bf["k_new"], bf["v_new"], res.num_accepted, self.start, self.tables(),
+                              n_commit_add=1, status=self.status)
         # next round: context grows by n, row 0 = the final token
         self.ctx.add_(res.num_accepted.clamp_min(0) + 1)
         idx = res.num_accepted.clamp_min(0).long().view(B, 1)

@@ -61,6 +61,28 @@ def _worker(rank, size, port, q):
         res["n"] = r.num_accepted.cpu().tolist()
         res["tok"] = r.tokens.cpu().tolist()
         res["tables"] = ver.tables().cpu().tolist()
+        # two micro-batches on two streams (one NCCL group each) == one batch, over 3 steps
+        B2 = 4
+        g2 = torch.Generator().manual_seed(8)
+        prompt2 = torch.randint(0, cfg.vocab, (B2, S0), generator=g2)
+        outs = []
+        for mb in (1, 2):
+            cache2 = m.make_cache(64, max_batch=B2)
+            v2 = BatchVerifier(m, cache2, list(range(B2)), K, micro_batches=mb)
+            v2.register_context(prompt2[:, :-1].tolist(), prompt2[:, -1])
+            v2.fill_synthetic_kv(torch.Generator(device=dev).manual_seed(3))
+            gd = torch.Generator(device=dev).manual_seed(9)
+            steps = []
+            for _ in range(3):
+                dt2 = torch.randint(0, cfg.vocab, (B2, K), generator=gd, device=dev, dtype=torch.int32)
+                dl2 = torch.randn(B2, K, cfg.vocab, generator=gd, device=dev).to(cfg.dtype)
+                u2 = torch.rand(B2, K + 1, generator=gd, device=dev) * 0.05
+                r2 = v2.step(dt2, dl2, u2)
+                torch.cuda.synchronize()
+                steps.append((r2.num_accepted.cpu().tolist(), r2.tokens.cpu().tolist()))
+            outs.append((v2.mb, steps, v2.tables().cpu().tolist(), cache2.key_pool.float().sum().item()))
+        res["mb_used"] = outs[1][0]
+        res["mb_equal"] = outs[0][1:] == outs[1][1:]
         q.put((rank, res))
     finally:
         dist.destroy_process_group()
@@ -82,3 +104,4 @@ def test_tp2_forward_and_step():
     assert out[0]["agree"]
     for key in ("n", "tok", "tables"):
         assert out[0][key] == out[1][key], key
+    assert out[0]["mb_used"] == 2 and out[0]["mb_equal"] and out[1]["mb_equal"]
