@@ -185,7 +185,28 @@ __global__ void splitk_rmsnorm_kernel(const float *part, int splits, int64_t pla
   const int m = blockIdx.x;
   T *yr = y + (int64_t)m * ldy;
   float ss = 0.0f;
-  for (int v = threadIdx.x; v < dim / 8; v += blockDim.x) {
+  constexpr int kKeep = 4;  // vectors of the row kept in registers for the second pass
+  uint4 kept[kKeep];
+  // the same per-thread order as cf_rmsnorm (vectors v = tid, tid + blockDim, ...): same sums
+#pragma unroll
+  for (int k = 0; k < kKeep; ++k) {
+    const int v = threadIdx.x + k * blockDim.x;
+    kept[k] = make_uint4(0, 0, 0, 0);
+    if (v >= dim / 8) continue;
+    float f8[8];
+    reduce8<T>(part, splits, plane, (int64_t)m * n + v * 8, res ? res + (int64_t)m * ldr + v * 8 : nullptr, f8);
+    uint4 o;
+    T *op = reinterpret_cast<T *>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) op[j] = from_f<T>(f8[j]);
+    reinterpret_cast<uint4 *>(yr)[v] = o;
+    kept[k] = o;
+    cf::Vec16<T> pk;
+    pk.raw = o;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { const float f = pk.get(j); ss += f * f; }
+  }
+  for (int v = threadIdx.x + kKeep * blockDim.x; v < dim / 8; v += blockDim.x) {  // very wide rows
     float f8[8];
     reduce8<T>(part, splits, plane, (int64_t)m * n + v * 8, res ? res + (int64_t)m * ldr + v * 8 : nullptr, f8);
     uint4 o;
@@ -211,16 +232,23 @@ __global__ void splitk_rmsnorm_kernel(const float *part, int splits, int64_t pla
   __syncthreads();
   const float inv = rsqrtf(red[0] / (float)dim + eps);
   T *orow = out + (int64_t)m * ldo;
-  for (int v = threadIdx.x; v < dim / 8; v += blockDim.x) {
+  auto norm_store = [&](int v, const uint4 raw) {
     cf::Vec16<T> pk, pw;
-    pk.raw = reinterpret_cast<const uint4 *>(yr)[v];  // this thread's own values, written above
+    pk.raw = raw;
     pw.raw = reinterpret_cast<const uint4 *>(w)[v];
     uint4 o;
     T *op = reinterpret_cast<T *>(&o);
 #pragma unroll
     for (int j = 0; j < 8; ++j) op[j] = from_f<T>(pk.get(j) * inv * pw.get(j));
     reinterpret_cast<uint4 *>(orow)[v] = o;
+  };
+#pragma unroll
+  for (int k = 0; k < kKeep; ++k) {
+    const int v = threadIdx.x + k * blockDim.x;
+    if (v < dim / 8) norm_store(v, kept[k]);
   }
+  for (int v = threadIdx.x + kKeep * blockDim.x; v < dim / 8; v += blockDim.x)
+    norm_store(v, reinterpret_cast<const uint4 *>(yr)[v]);  // this thread's own values, written above
 }
 
 // The RoPE / K-V scatter of rope_qkv_kernel on T(sum of partials); rotated q goes to qkv.
