@@ -17,14 +17,15 @@
 //   halves, two TMEM accumulators) x one K split x one token slice, so each
 //   token tile the SM pulls through its TMA path feeds 256 weight rows: the
 //   per-SM TMA path (~100 GB/s from L2, ~0.1-0.3 us per op from one issuing
-//   thread, measured) is what the tile shape is sized against.  7 warps:
+//   thread, measured) is what the tile shape is sized against.  19 warps:
 //     warp 0      weight producer (lane 0 packed W, lane 1 group scales)
-//     warp 1      TMEM allocator + MMA issue (whole warp, elect.sync lane)
-//     warps 2-9   INT4 -> bf16 dequantisation into the 128-B swizzled A
-//                 tiles (one weight row per thread), then the epilogue
+//     warp 1      TMEM allocator + MMA issue (one thread)
+//     warps 2-17  INT4 -> bf16 dequantisation straight into TMEM (one weight
+//                 row per thread; two groups of 8 warps take alternate
+//                 stages), then the epilogue
 //                 (tcgen05.ld -> shared staging -> 16-byte row-contiguous
 //                 stores)
-//     warp 10     token-tile producer
+//     warp 18     token-tile producer
 //   Three independent rings (packed W, dequantised A, token tile), every
 //   mbarrier wait bounded (a device status word records CF_ETIMEOUT), no TMA
 //   multicast.
@@ -43,7 +44,9 @@ namespace {
 
 using namespace cf::sm100;
 
-constexpr int kThreads = 352;  // 11 warps
+constexpr int kDqGroups = 2;                    // dequantisation warp groups (8 warps each, alternate stages)
+constexpr int kXWarp = 2 + 8 * kDqGroups;       // token-tile producer warp
+constexpr int kThreads = (kXWarp + 1) * 32;     // 19 warps
 constexpr int HN = 128;        // weight rows per MMA (tcgen05 M)
 constexpr int TN = 256;        // weight rows per CTA (two MMA halves)
 constexpr int BK = 64;         // k per pipeline stage: one 128-B swizzle atom of 16-bit elements
@@ -64,6 +67,7 @@ struct GemmParams {
   int sa, sx, sw;                  // ring depths: dequantised A, token tile X, packed W (+scales)
   uint32_t off_x, off_w, off_bar;  // ring bases (A ring at 0)
   uint32_t x_bytes;
+  int x_box;                       // token rows per TMA box (divides m_slice)
   uint32_t tmem_cols, idesc;
   uint32_t a_tcol;                 // INT4: first TMEM column of the dequantised-A stages
   void *y;
@@ -109,6 +113,51 @@ template <typename T> __device__ __forceinline__ T from_f(float v);
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
+// Optional per-role timeline of CTA (0,0,0) (cf_gemm_args.trace).
+#define CF_TRACE(role, i) \
+  if (tr && (i) < 512) p.trace[(role) * 512 + (i)] = clock64()
+
+// MMA issue of one CTA (one thread): per 64-k stage, 4 k-steps x H weight-row halves.
+template <int WM, int H>
+__device__ __forceinline__ bool mma_loop(const GemmParams &p, uint32_t tmem, uint8_t *a_ring, uint8_t *x_ring,
+                                         uint64_t *afull, uint64_t *xfull, uint64_t *aempty, uint64_t *xempty,
+                                         int nkb, bool tr) {
+  const uint32_t idesc = p.idesc;
+  const int SA = p.sa, SX = p.sx;
+  int sa = 0, sx = 0;
+  uint32_t pa = 0, px = 0;
+  for (int i = 0; i < nkb; ++i) {
+    CF_TRACE(6, i);
+    if (!mbar_wait(&afull[sa], pa, p.timeout_ns)) return false;
+    CF_TRACE(7, i);
+    if (!mbar_wait(&xfull[sx], px, p.timeout_ns)) return false;
+    tc_fence_after();
+    const uint32_t a_base = smem_u32(a_ring + sa * kAStageBytes);
+    const uint32_t x_base = smem_u32(x_ring + sx * p.x_bytes);
+    const uint32_t at0 = tmem + p.a_tcol + (uint32_t)(sa * 64);
+    CF_TRACE(3, i);
+#pragma unroll
+    for (int k16 = 0; k16 < BK / 16; ++k16) {
+      const uint64_t bd = desc_kmajor_sw128(x_base + k16 * 32);
+      const uint32_t acc = (i > 0 || k16 > 0) ? 1u : 0u;
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        if (WM == kInt4)  // A from TMEM: 32 columns per half per stage, 8 per k16
+          mma_f16_ts(tmem + (uint32_t)(h * p.m_slice), at0 + (uint32_t)(h * 32 + k16 * 8), bd, idesc, acc);
+        else
+          mma_f16(tmem + (uint32_t)(h * p.m_slice), desc_kmajor_sw128(a_base + h * kHalfBytes + k16 * 32), bd, idesc,
+                  acc);
+      }
+    }
+    mma_commit(&aempty[sa]);
+    mma_commit(&xempty[sx]);
+    CF_TRACE(8, i);
+    if (++sa == SA) { sa = 0; pa ^= 1u; }
+    if (++sx == SX) { sx = 0; px ^= 1u; }
+  }
+  return true;
+}
+
 template <typename T, int WM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
@@ -142,8 +191,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   const int rot = nkb > 0 ? (int)((blockIdx.y * 7u + blockIdx.x * 3u) % (unsigned)nkb) : 0;
   auto kb_of = [&](int i) { int j = i + rot; return kb0 + (j >= nkb ? j - nkb : j); };
   const bool tr = p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
-#define CF_TRACE(role, i) \
-  if (tr && (i) < 512) p.trace[(role) * 512 + (i)] = clock64()
 
   // set when any role's bounded wait ran out: every role then drains before TMEM is freed
   volatile int &s_fail = *reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -198,81 +245,60 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       __syncwarp();
       issued_w = i + 1;
     }
-  } else if (warp == 10) {
+  } else if (warp == kXWarp) {
     // ---------------- token-tile producer ----------------
     for (int i = 0; i < nkb; ++i) {
       const int s = i % SX;
       const uint32_t ph = (uint32_t)(i / SX) & 1u;
       if (i >= SX && !mbar_wait_warp(&xempty[s], ph ^ 1u, p.timeout_ns)) { ok = false; break; }
       const int kb = kb_of(i);
-      // one 16-row box (2 KB, 1024-B aligned) per lane: a single issuing thread
-      // sustains only ~30 GB/s of TMA traffic, many lanes in parallel far more
+      // boxes of x_box token rows (x_box * 128 B, 1024-B aligned; the 128-B swizzle
+      // pattern repeats every 8 rows, so any multiple of 8 rows gives the layout of one
+      // tile), one per lane, rotating over the lanes per stage.  The per-SM TMA unit is
+      // bound by operations more than bytes: few large boxes feed it fastest.
       if (lane == 0) {
         CF_TRACE(4, i);
         mbar_arrive_expect_tx(&xfull[s], p.x_bytes);
       }
       __syncwarp();
       {
-        const int nbox = p.m_slice / 16;
+        const int nbox = p.m_slice / p.x_box;
         const int b = (lane - i * nbox) & 31;  // box handled by this lane (rotating per stage)
         if (b < nbox)
-          tma_load_2d(x_ring + s * p.x_bytes + b * 2048, &tm_x, &xfull[s], kb * BK, m0 + b * 16);
+          tma_load_2d(x_ring + s * p.x_bytes + b * p.x_box * 128, &tm_x, &xfull[s], kb * BK, m0 + b * p.x_box);
       }
       __syncwarp();
       issued_x = i + 1;
     }
   } else if (warp == 1) {
     // ---------------- MMA issue: one thread; ring slots and phases advance by increments ----------------
+    // The stage's MMAs are a compile-time unrolled block (the number of halves is a
+    // template argument): measured on B200, a runtime-bounded loop around tcgen05.mma
+    // and tcgen05.commit ran at 250-450 cycles per MMA, the unrolled block at the
+    // tensor pipe's rate (~96 cycles at M=128, N=192, K=16).
     if (lane == 0) {
-      const uint32_t idesc = p.idesc;
-      int sa = 0, sx = 0;
-      uint32_t pa = 0, px = 0;
-      for (int i = 0; i < nkb; ++i) {
-        CF_TRACE(6, i);
-        if (!mbar_wait(&afull[sa], pa, p.timeout_ns)) { ok = false; break; }
-        CF_TRACE(7, i);
-        if (!mbar_wait(&xfull[sx], px, p.timeout_ns)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(a_ring + sa * kAStageBytes);
-        const uint32_t x_base = smem_u32(x_ring + sx * p.x_bytes);
-        CF_TRACE(3, i);
-#pragma unroll
-        for (int k16 = 0; k16 < BK / 16; ++k16) {
-          const uint64_t bd = desc_kmajor_sw128(x_base + k16 * 32);
-          for (int h = 0; h < halves; ++h) {
-            const uint32_t acc = (i > 0 || k16 > 0) ? 1u : 0u;
-            if (WM == kInt4) {  // A from TMEM: 32 columns per half per stage, 8 per k16
-              const uint32_t at = tmem + p.a_tcol + (uint32_t)((sa * 2 + h) * 32 + k16 * 8);
-              mma_f16_ts(tmem + (uint32_t)(h * p.m_slice), at, bd, idesc, acc);
-            } else {
-              const uint64_t ad = desc_kmajor_sw128(a_base + h * kHalfBytes + k16 * 32);
-              mma_f16(tmem + (uint32_t)(h * p.m_slice), ad, bd, idesc, acc);
-            }
-          }
-        }
-        mma_commit(&aempty[sa]);
-        mma_commit(&xempty[sx]);
-        CF_TRACE(8, i);
-        if (++sa == SA) { sa = 0; pa ^= 1u; }
-        if (++sx == SX) { sx = 0; px ^= 1u; }
-      }
+      if (halves == 2) ok = mma_loop<WM, 2>(p, tmem, a_ring, x_ring, afull, xfull, aempty, xempty, nkb, tr);
+      else ok = mma_loop<WM, 1>(p, tmem, a_ring, x_ring, afull, xfull, aempty, xempty, nkb, tr);
       mma_commit(accf);  // completes when every issued MMA has finished
     }
     __syncwarp();
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
   } else {
-    // ---------------- dequantisation (warps 2-9) straight into TMEM ----------------
+    // ---------------- dequantisation (warps 2-17) straight into TMEM ----------------
     // Warp w may only touch TMEM lanes 32*(w%4)..+31, so warp w owns rows
-    // (w%4)*32 + lane of half h = (w-2)/4; each thread dequantises its row's
-    // 64 k values and stores them with one tcgen05.st (32 columns).
-    const int q = warp & 3, h = (warp - 2) >> 2;
+    // (w%4)*32 + lane of half h = ((w-2)/4)%2; each thread dequantises its row's
+    // 64 k values and stores them with one tcgen05.st (32 columns).  Group
+    // g = (w-2)/8 takes the stages i = g (mod 2): one group's dequantisation of a stage
+    // (~850 cycles, latency-bound at two warps per SM sub-partition) overlaps the other's.
+    const int q = warp & 3, h = ((warp - 2) >> 2) & 1, g = (warp - 2) >> 3;
     const int row = q * 32 + lane;  // within the half == TMEM lane
     const int t = h * HN + row;     // within the 256-row tile
     if (WM == kInt4) {
-      for (int i = 0; i < nkb; ++i) {
-        const int sw = i % SW, sa = i % SA;
+      for (int i = g; i < nkb; i += kDqGroups) {
+        const int sw = i % SW;
         // warp-uniform waits: a lane must not leave the loop while the others reach __syncwarp
         if (!mbar_wait_warp(&wfull[sw], (uint32_t)(i / SW) & 1u, p.timeout_ns)) { ok = false; break; }
+        if (threadIdx.x == 64) CF_TRACE(9, i);
         const uint8_t *st = w_ring + sw * kWStageBytes;
         const uint32_t *wp = reinterpret_cast<const uint32_t *>(st);
         const float sf = __half2float(reinterpret_cast<const __half *>(st + kWPackBytes)[t]);
@@ -288,6 +314,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         __syncwarp();
         if (lane == 0) mbar_arrive(&wempty[sw]);  // packed words are consumed
         // dequantised into registers first: only the TMEM store waits for the A slot
+        const int sa = i % SA;
+        if (threadIdx.x == 64) CF_TRACE(10, i);
         if (i >= SA && !mbar_wait_warp(&aempty[sa], ((uint32_t)(i / SA) & 1u) ^ 1u, p.timeout_ns)) { ok = false; break; }
         tc_fence_after();
         if (threadIdx.x == 64) CF_TRACE(1, i);
@@ -311,9 +339,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       float *stg = reinterpret_cast<float *>(a_ring + (warp - 2) * 4096);  // [32 tokens][32 n]
       T *y = reinterpret_cast<T *>(p.y);
       const T *res = reinterpret_cast<const T *>(p.residual);
-      if (h < halves) {  // warps 2-5 drain half 0, warps 6-9 half 1
+      if (h < halves) {  // per group: 4 warps drain half 0, 4 half 1; the groups alternate 32-token chunks
         const int nw = n0 + h * HN + q * 32;
-        for (int c = 0; c < mrows; c += 32) {
+        for (int c = 32 * g; c < mrows; c += 32 * kDqGroups) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * p.m_slice + c), r);
           tmem_ld_wait();
@@ -362,7 +390,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
       uint64_t *fullb = WM == kInt4 ? wfull : afull;
       for (int j = max(0, issued_w - S); j < issued_w; ++j)
         mbar_wait_warp(&fullb[j % S], (uint32_t)(j / S) & 1u, kDrainNs);
-    } else if (warp == 10) {
+    } else if (warp == kXWarp) {
       for (int j = max(0, issued_x - SX); j < issued_x; ++j)
         mbar_wait_warp(&xfull[j % SX], (uint32_t)(j / SX) & 1u, kDrainNs);
     } else if (warp == 1) {
@@ -418,7 +446,7 @@ __global__ void repack_kernel(const uint32_t *src, uint32_t *dst, int64_t n_word
 }
 
 struct Plan {
-  int slices, m_slice, splits, kb_per_split, sa, sx, sw, ntiles;
+  int slices, m_slice, splits, kb_per_split, sa, sx, sw, ntiles, x_box;
   uint32_t x_bytes, off_x, off_w, off_bar, tmem_cols, a_tcol;
   size_t smem;
 };
@@ -438,9 +466,10 @@ bool make_plan(int M, int N, int K, int split_req, bool int4, Plan &pl) {
   const int max_slice = int4 ? 192 : kMaxSlice;
   pl.slices = (M + max_slice - 1) / max_slice;
   const int per = (M + pl.slices - 1) / pl.slices;
-  pl.m_slice = (per + 15) / 16 * 16;  // loaded as m_slice/16 boxes of 16 rows
+  pl.m_slice = (per + 15) / 16 * 16;
   if (pl.m_slice > max_slice) return false;
-  // smem: A ring (dense: 32 KB / stage; INT4: 32 KB epilogue staging) | X ring | W ring (8.5 KB / stage)
+  pl.x_box = pl.m_slice;  // one TMA box per token tile (box rows <= 256)
+  // smem: A ring (dense: 32 KB / stage; INT4: 64 KB epilogue staging) | X ring | W ring (8.5 KB / stage)
   pl.x_bytes = (uint32_t)pl.m_slice * 128u;
   const size_t budget = kMaxSmem - 1024 - 1024;  // alignment slack + barriers
   const size_t w_stage = int4 ? kWStageBytes : 0;
@@ -452,12 +481,14 @@ bool make_plan(int M, int N, int K, int split_req, bool int4, Plan &pl) {
     pl.a_tcol = 0;
     pl.sa = 3;
   }
-  const size_t a_bytes = int4 ? (size_t)kAStageBytes : pl.sa * (size_t)kAStageBytes;
+  // INT4: the A ring's smem is only the epilogue staging, 4 KB per dequantisation warp
+  const size_t stage_bytes = (size_t)kDqGroups * 8 * 4096;
+  const size_t a_bytes = int4 ? stage_bytes : pl.sa * (size_t)kAStageBytes;
   pl.sw = int4 ? 8 : 1;
   pl.sx = (int)std::min<size_t>(6, (budget - a_bytes - pl.sw * w_stage) / pl.x_bytes);
   if (pl.sx < 2 && !int4) { pl.sa = 2; pl.sx = (int)std::min<size_t>(4, (budget - 2 * (size_t)kAStageBytes) / pl.x_bytes); }
   if (pl.sx < 2 || pl.sa < 2 || (int4 && pl.sw < 2)) return false;
-  pl.off_x = (uint32_t)(int4 ? kAStageBytes : pl.sa * kAStageBytes);
+  pl.off_x = (uint32_t)a_bytes;
   pl.off_w = pl.off_x + pl.sx * pl.x_bytes;
   pl.off_bar = (pl.off_w + (int4 ? pl.sw * kWStageBytes : 0) + 15u) & ~15u;
   pl.smem = 1024 + pl.off_bar + 8 * (2 * pl.sw + 2 * pl.sx + 2 * pl.sa + 1) + 16;
@@ -501,7 +532,7 @@ int run_gemm(const cf_gemm_args &a, cudaStream_t stream, bool partials_only = fa
   const CUtensorMapDataType tdt =
       std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tx, tw, ts;
-  if (!cf::make_tmap_2d(&tx, tdt, a.x, (uint64_t)a.k, (uint64_t)a.m, (uint64_t)a.ldx * 2, BK, 16,
+  if (!cf::make_tmap_2d(&tx, tdt, a.x, (uint64_t)a.k, (uint64_t)a.m, (uint64_t)a.ldx * 2, BK, (uint32_t)pl.x_box,
                         CU_TENSOR_MAP_SWIZZLE_128B))
     return CF_EINVAL;
   if (int4) {
@@ -522,6 +553,7 @@ int run_gemm(const cf_gemm_args &a, cudaStream_t stream, bool partials_only = fa
   p.m_slice = pl.m_slice;
   p.kb_per_split = pl.kb_per_split; p.splits = pl.splits;
   p.sa = pl.sa; p.sx = pl.sx; p.sw = pl.sw;
+  p.x_box = pl.x_box;
   p.off_x = pl.off_x; p.off_w = pl.off_w; p.off_bar = pl.off_bar; p.x_bytes = pl.x_bytes;
   p.tmem_cols = pl.tmem_cols;
   p.a_tcol = pl.a_tcol;

@@ -230,8 +230,11 @@ typedef struct cf_gemm_args {
   size_t workspace_bytes;
   int32_t *status;       /* optional */
   uint64_t timeout_ns;   /* 0 = default */
-  uint64_t *trace;       /* optional profiling aid: [6][512] global-timer stamps of CTA 0
-                            (W issue, dequant start/end, MMA issue, X issue, epilogue) */
+  uint64_t *trace;       /* optional profiling aid: [11][512] SM-clock stamps of CTA (0,0,0)
+                            per 64-k stage and role: 0 W issue, 1 dequant TMEM store start,
+                            2 dequant arrive, 3 MMA issue start, 4 X issue, 5 epilogue
+                            start/end, 6-7 MMA waits, 8 MMA commits, 9 dequant W ready,
+                            10 dequant computed */
 } cf_gemm_args;
 
 size_t cf_gemm_workspace_bytes(int32_t m, int32_t n, int32_t k, int32_t split_k, int32_t int4);
