@@ -122,19 +122,23 @@ template <int WM, int H>
 __device__ __forceinline__ bool mma_loop(const GemmParams &p, uint32_t tmem, uint8_t *a_ring, uint8_t *x_ring,
                                          uint64_t *afull, uint64_t *xfull, uint64_t *aempty, uint64_t *xempty,
                                          int nkb, bool tr) {
+  // parameters copied to registers once: every inline-asm statement below clobbers
+  // memory, which would otherwise force a reload of each field after every MMA
   const uint32_t idesc = p.idesc;
   const int SA = p.sa, SX = p.sx;
+  const uint32_t m_slice = (uint32_t)p.m_slice, a_tcol = p.a_tcol, x_bytes = p.x_bytes;
+  const uint64_t limit = p.timeout_ns;
   int sa = 0, sx = 0;
   uint32_t pa = 0, px = 0;
   for (int i = 0; i < nkb; ++i) {
     CF_TRACE(6, i);
-    if (!mbar_wait(&afull[sa], pa, p.timeout_ns)) return false;
+    if (!mbar_wait(&afull[sa], pa, limit)) return false;
     CF_TRACE(7, i);
-    if (!mbar_wait(&xfull[sx], px, p.timeout_ns)) return false;
+    if (!mbar_wait(&xfull[sx], px, limit)) return false;
     tc_fence_after();
     const uint32_t a_base = smem_u32(a_ring + sa * kAStageBytes);
-    const uint32_t x_base = smem_u32(x_ring + sx * p.x_bytes);
-    const uint32_t at0 = tmem + p.a_tcol + (uint32_t)(sa * 64);
+    const uint32_t x_base = smem_u32(x_ring + sx * x_bytes);
+    const uint32_t at0 = tmem + a_tcol + (uint32_t)(sa * 64);
     CF_TRACE(3, i);
 #pragma unroll
     for (int k16 = 0; k16 < BK / 16; ++k16) {
@@ -143,13 +147,14 @@ __device__ __forceinline__ bool mma_loop(const GemmParams &p, uint32_t tmem, uin
 #pragma unroll
       for (int h = 0; h < H; ++h) {
         if (WM == kInt4)  // A from TMEM: 32 columns per half per stage, 8 per k16
-          mma_f16_ts(tmem + (uint32_t)(h * p.m_slice), at0 + (uint32_t)(h * 32 + k16 * 8), bd, idesc, acc);
+          mma_f16_ts(tmem + (uint32_t)h * m_slice, at0 + (uint32_t)(h * 32 + k16 * 8), bd, idesc, acc);
         else
-          mma_f16(tmem + (uint32_t)(h * p.m_slice), desc_kmajor_sw128(a_base + h * kHalfBytes + k16 * 32), bd, idesc,
+          mma_f16(tmem + (uint32_t)h * m_slice, desc_kmajor_sw128(a_base + h * kHalfBytes + k16 * 32), bd, idesc,
                   acc);
       }
     }
-    mma_commit(&aempty[sa]);
+    // one commit per stage: xempty[] is the ring of stage-done barriers that the token
+    // producer and the A-slot writers both wait on (depth SX >= SA)
     mma_commit(&xempty[sx]);
     CF_TRACE(8, i);
     if (++sa == SA) { sa = 0; pa ^= 1u; }
@@ -191,6 +196,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
   const int rot = nkb > 0 ? (int)((blockIdx.y * 7u + blockIdx.x * 3u) % (unsigned)nkb) : 0;
   auto kb_of = [&](int i) { int j = i + rot; return kb0 + (j >= nkb ? j - nkb : j); };
   const bool tr = p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+  if (threadIdx.x == 0) CF_TRACE(5, 2);  // kernel entry
 
   // set when any role's bounded wait ran out: every role then drains before TMEM is freed
   volatile int &s_fail = *reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -223,7 +229,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
     for (int i = 0; i < nkb; ++i) {
       const int s = i % S;
       const uint32_t ph = (uint32_t)(i / S) & 1u;
-      if (i >= S && !mbar_wait_warp(&emptyb[s], ph ^ 1u, p.timeout_ns)) { ok = false; break; }
+      if (WM == kInt4) {
+        if (i >= S && !mbar_wait_warp(&emptyb[s], ph ^ 1u, p.timeout_ns)) { ok = false; break; }
+      } else if (i >= SA) {  // dense: A slot s is free once stage i - SA is done
+        const int j = i - SA;
+        if (!mbar_wait_warp(&xempty[j % SX], (uint32_t)(j / SX) & 1u, p.timeout_ns)) { ok = false; break; }
+      }
       const int kb = kb_of(i);
       if (lane == 0) {
         CF_TRACE(0, i);
@@ -316,7 +327,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CU
         // dequantised into registers first: only the TMEM store waits for the A slot
         const int sa = i % SA;
         if (threadIdx.x == 64) CF_TRACE(10, i);
-        if (i >= SA && !mbar_wait_warp(&aempty[sa], ((uint32_t)(i / SA) & 1u) ^ 1u, p.timeout_ns)) { ok = false; break; }
+        // A slot sa is free once stage i - SA is done (the stage-done ring has depth SX >= SA)
+        if (i >= SA && !mbar_wait_warp(&xempty[(i - SA) % SX], (uint32_t)((i - SA) / SX) & 1u, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         if (threadIdx.x == 64) CF_TRACE(1, i);
         if (h < halves)
@@ -488,6 +503,7 @@ bool make_plan(int M, int N, int K, int split_req, bool int4, Plan &pl) {
   pl.sx = (int)std::min<size_t>(6, (budget - a_bytes - pl.sw * w_stage) / pl.x_bytes);
   if (pl.sx < 2 && !int4) { pl.sa = 2; pl.sx = (int)std::min<size_t>(4, (budget - 2 * (size_t)kAStageBytes) / pl.x_bytes); }
   if (pl.sx < 2 || pl.sa < 2 || (int4 && pl.sw < 2)) return false;
+  pl.sa = std::min(pl.sa, pl.sx);  // stage-done barriers live in the X ring (depth SX >= SA)
   pl.off_x = (uint32_t)a_bytes;
   pl.off_w = pl.off_x + pl.sx * pl.x_bytes;
   pl.off_bar = (pl.off_w + (int4 ? pl.sw * kWStageBytes : 0) + 15u) & ~15u;
