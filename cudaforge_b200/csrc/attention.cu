@@ -26,6 +26,13 @@
 #include "sm100.cuh"
 #include "tmap.h"
 
+namespace cf {
+namespace attn_tc {  // attention_tc.cu: tcgen05 path for >= 128 rows per kv head
+bool eligible(const cf_attn_args &a);
+int launch(const cf_attn_args &a, cudaStream_t stream);
+}  // namespace attn_tc
+}  // namespace cf
+
 #include <algorithm>
 #include <cstdlib>
 #include <math.h>
@@ -555,6 +562,7 @@ int dispatch(const cf_attn_args &a, cudaStream_t s) {
 
 extern "C" size_t cf_attention_workspace_bytes(const cf_attn_args *a) {
   if (!a || a->kv.num_kv_heads <= 0 || a->num_q_heads % a->kv.num_kv_heads) return 0;
+  if (cf::attn_tc::eligible(*a)) return 0;
   const int G = a->num_q_heads / a->kv.num_kv_heads;
   const int rows_total = a->rows * G;
   const int mt = attn_mt(rows_total);
@@ -578,6 +586,7 @@ extern "C" int cf_verify_attention(const cf_attn_args *args, void *stream) {
       (reinterpret_cast<uintptr_t>(a.k_new) & 15) || (reinterpret_cast<uintptr_t>(a.v_new) & 15))
     return CF_EINVAL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cf::attn_tc::eligible(a)) return cf::attn_tc::launch(a, s);
   if (a.kv.dtype == CF_BF16) return dispatch<__nv_bfloat16>(a, s);
   if (a.kv.dtype == CF_F16) return dispatch<__half>(a, s);
   return CF_EUNSUPPORTED;

@@ -140,6 +140,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int32_t x, int32_t y,
+                                            int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -243,6 +252,16 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// Thread t of the warp writes row (lane base + t), 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -257,6 +276,20 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
   d |= (uint64_t)(1024u >> 4) << 32;            // stride byte offset: 8 rows * 128 B
   d |= (uint64_t)1u << 46;                      // descriptor version (sm_100)
   d |= (uint64_t)2u << 61;                      // SWIZZLE_128B
+  return d;
+}
+
+// Shared-memory matrix descriptor, MN-major operand, 128-byte swizzle: 8 K-rows x
+// 128 B (64 MN elements) atoms; `mn_atom_bytes` apart along MN, `k_group_bytes`
+// apart per 8 K-rows.  Used with the instruction descriptor's transpose bit.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t smem_addr, uint32_t mn_atom_bytes,
+                                                       uint32_t k_group_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((mn_atom_bytes >> 4) & 0x3FFFu) << 16;  // leading byte offset
+  d |= (uint64_t)((k_group_bytes >> 4) & 0x3FFFu) << 32;  // stride byte offset
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
   return d;
 }
 

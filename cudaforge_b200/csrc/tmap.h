@@ -41,4 +41,21 @@ inline bool make_tmap_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *bas
   return r == CUDA_SUCCESS;
 }
 
+// 3-D tiled map: dim0 (contiguous) x dim1 x dim2, pitches in bytes for dims 1 and 2.
+inline bool make_tmap_3d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t dim0, uint64_t dim1,
+                         uint64_t dim2, uint64_t pitch1_bytes, uint64_t pitch2_bytes, uint32_t box0, uint32_t box1,
+                         uint32_t box2, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (pitch1_bytes & 15) != 0 || (pitch2_bytes & 15) != 0)
+    return false;
+  cuuint64_t dims[3] = {dim0, dim1, dim2};
+  cuuint64_t strides[2] = {pitch1_bytes, pitch2_bytes};
+  cuuint32_t box[3] = {box0, box1, box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace cf

@@ -210,6 +210,10 @@ class TreeVerifier:
         self.ws = torch.empty(_lib.lib().cf_accept_tree_workspace_bytes(b.B, N1, V) + 256, dtype=torch.uint8,
                               device=dev)
 
+    @property
+    def seq_ids(self):
+        return self.base.seq_ids
+
     def register_context(self, prompts, last_tokens) -> None:
         self.base.register_context(prompts, last_tokens)
 

@@ -86,6 +86,51 @@ def test_verify_attention_tree_mask(splits):
     assert (out.view(B, R, Hq, D).float() - ref).abs().max().item() < 2e-2
 
 
+@pytest.mark.parametrize("qscale", [1.0, 6.0])
+def test_verify_attention_tcgen05_wide_tree(qscale):
+    """>= 128 rows per kv head (65 tree rows x 4 heads) take the tcgen05 path
+    (attention_tc.cu): long contexts (several 128-key blocks, ring wrap-around,
+    partial last blocks, an empty context), a random tree mask, and scaled-up
+    queries that force the lazy running-max rescale of O.  Checked against the
+    fp32 restatement and against the warp-MMA kernel (selected by an explicit
+    KV split)."""
+    D, Hq, Hkv, R, L = 128, 32, 8, 65, 2
+    ctxs = [1500, 129, 0, 2048]
+    B = len(ctxs)
+    c = _cache(L, Hkv, D, sum((n + R) // 16 + 2 for n in ctxs) + 8, seed=5)
+    for i, n in enumerate(ctxs):
+        c.register_sequence_with_prefix(i, list(range(n)))
+    tables, ctx = c.prepare_batch_metadata(list(range(B)))
+    g = torch.Generator().manual_seed(11)
+    mask = torch.zeros(B, R, R, dtype=torch.bool)
+    for b in range(B):
+        par = [-1] + [int(torch.randint(0, j, (1,), generator=g)) for j in range(1, R)]
+        for j in range(R):
+            k = j
+            while k >= 0:
+                mask[b, j, k] = True
+                k = par[k]
+    bits = (mask.to(torch.int64) << torch.arange(64).repeat(2)[:R].view(1, 1, R))  # bit j % 64
+    words = torch.stack([bits[..., :64].sum(-1), bits[..., 64:].sum(-1)], -1)
+    gq = torch.Generator(device="cuda").manual_seed(12)
+    q = (torch.randn(B * R, Hq * D, generator=gq, device="cuda") * qscale).to(torch.bfloat16)
+    kn = torch.randn(B, R, Hkv, D, generator=gq, device="cuda").to(torch.bfloat16)
+    vn = torch.randn(B, R, Hkv, D, generator=gq, device="cuda").to(torch.bfloat16)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kw = dict(rows=R, num_q_heads=Hq, tree_mask=words.cuda(), status=st)
+    out = ops.verify_attention(c, 1, q, kn, vn, tables, ctx, max(ctxs), **kw).clone()
+    old = ops.verify_attention(c, 1, q, kn, vn, tables, ctx, max(ctxs), num_splits=2, **kw)
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    kp, vp = _pool5(c)
+    ref = llama_ref.verify_attention(q.view(B, R, Hq, D), kp, vp, 1, tables.cpu(), ctx.cpu(), kn, vn,
+                                     tree_mask=mask.cuda())
+    err = (out.view(B, R, Hq, D).float() - ref).abs().max().item()
+    err_old = (old.view(B, R, Hq, D).float() - ref).abs().max().item()
+    print(f"tcgen05 tree attention max-abs {err:.3e} (warp-MMA kernel {err_old:.3e})")
+    assert err < 2e-2 and err_old < 2e-2
+
+
 def test_kv_commit_chain_and_tree():
     L, Hkv, D, B, R = 3, 2, 128, 4, 6
     c = _cache(L, Hkv, D, 40)
