@@ -15,16 +15,19 @@
 //   this step's new rows);
 //   S_j = Q K_j^T   tcgen05.mma, A = Q (smem, K-major), B = K block (smem,
 //                   K-major), D = S buffer j%2 in TMEM (128 x 128 fp32);
-//   softmax         4 warps, one query row per thread (TMEM lane): row max,
-//                   2^(s*scale*log2e - m), row sum, P_j as bf16 into TMEM;
-//                   the running max is raised lazily (only when a block's max
-//                   exceeds it by more than 2^8), rescaling O in TMEM then;
-//   O += P_j V_j    tcgen05.mma, A = P_j (TMEM), B = V block (smem, MN-major),
-//                   D = O in TMEM (128 x 128 fp32);
-//   output          O / l, bf16, by the softmax warps.
-// TMEM: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
-// Warps: 0 K producer and 6 V producer (TMA page boxes; the new rows as one 3-D box each),
-// 1 TMEM allocator + MMA issue (one thread), 2-5 softmax / output.  Every
+//   softmax         two groups of 4 warps take alternate blocks (two softmax warps
+//                   per SM sub-partition hide each other's latency); one query row
+//                   per thread (TMEM lane): row max, 2^(s*scale*log2e - m), row
+//                   sum, P_j as bf16 written over S_j's first 64 columns; each group
+//                   keeps its own running max, sum and O, raising the max lazily
+//                   (only when a block's max exceeds it by more than 2^8, rescaling
+//                   that group's O in TMEM then);
+//   O_g += P_j V_j  tcgen05.mma, A = P_j (TMEM), B = V block (smem, MN-major),
+//                   D = O of group g = j % 2 in TMEM (128 x 128 fp32);
+//   output          the two groups merged per row in log-sum-exp form, O / l, bf16.
+// TMEM: S/P buffer 0 [0,128), 1 [128,256), O of group 0 [256,384), group 1 [384,512).
+// Warps: 0 K producer and 10 V producer (TMA page boxes; the new rows as one 3-D box
+// each), 1 TMEM allocator + MMA issue (one thread), 2-5 and 6-9 softmax groups.  Every
 // mbarrier wait is bounded (CF_ETIMEOUT in the status word); no multicast.
 #include "common.cuh"
 #include "sm100.cuh"
@@ -42,11 +45,12 @@ constexpr int HD = 128;                   // head dim (two 64-column swizzle ato
 constexpr int kRows = 128;                // query rows per CTA (TMEM lanes)
 constexpr int kKeys = 128;                // keys per block (8 pages)
 constexpr int kStages = 3;                // K/V block ring (3 x 64 KB + Q 32 KB)
-constexpr int kThreads = 7 * 32;
+constexpr int kThreads = 11 * 32;
+constexpr int kVWarp = 10;               // V producer warp
 constexpr uint32_t kTileBytes = kKeys * HD * 2;  // 32 KB: one tensor, one block
 constexpr uint32_t kBoxBytes = kKeys * 128;      // 16 KB: 64 columns of one block
 constexpr uint32_t kQBytes = kRows * HD * 2;     // 32 KB
-constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
+constexpr uint32_t kColS = 0, kColO = 256;  // S/P buffer g at 128 g, O of group g at 256 + 128 g
 constexpr float kLazy = 8.0f;             // log2 headroom before the running max is raised
 constexpr uint64_t kDrainNs = 1000000000ull;
 
@@ -95,9 +99,8 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   uint64_t *kv_full = reinterpret_cast<uint64_t *>(kv_s + kStages * 2 * kTileBytes);  // [K, V][stage]
   uint64_t *kv_empty = kv_full + 2 * kStages;  // K slot freed by QK_j, V slot by PV_j
   uint64_t *s_full = kv_empty + 2 * kStages;   // [2] QK_j done -> S buffer j%2 readable
-  uint64_t *p_full = s_full + 2;           // [2] P_j in TMEM (4 softmax warps arrive)
-  uint64_t *pv_done = p_full + 2;          // [2] PV_j done (P buffer j%2 free, O updated)
-  uint64_t *o_done = pv_done + 2;          // every MMA of the CTA done
+  uint64_t *p_full = s_full + 2;           // [2] P_j in TMEM (the 4 warps of group j%2 arrive)
+  uint64_t *o_done = p_full + 2;           // every MMA of the CTA done
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_done + 1);
   volatile int &s_fail = *reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -129,7 +132,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   if (threadIdx.x == 0) {
     s_fail = 0;
     for (int s = 0; s < 2 * kStages; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&p_full[s], 4); mbar_init(&pv_done[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&s_full[s], 1); mbar_init(&p_full[s], 4); }
     mbar_init(o_done, 1);
     fence_mbar_init();
   }
@@ -142,10 +145,10 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
   int issued = 0;  // key blocks whose TMA loads this producer started (drained on failure)
-  const int tv = warp == 6 ? 1 : 0;  // producer warps: the tensor they load
+  const int tv = warp == kVWarp ? 1 : 0;  // producer warps: the tensor they load
 
-  if (warp == 0 || warp == 6) {
-    // ---------------- K (warp 0) / V (warp 6) producer ----------------
+  if (warp == 0 || warp == kVWarp) {
+    // ---------------- K (warp 0) / V (warp 10) producer ----------------
     const int pool_rows_per_block = p.L * p.Hkv * kPage;
     for (int j = 0; j < nb; ++j) {
       const int s = j % kStages;
@@ -188,8 +191,9 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     }
   } else if (warp == 1) {
     // ---------------- MMA issue (one thread) ----------------
-    // Order: QK_0; then per block j: QK_{j+1} (its S buffer was released by the softmax of
-    // block j-1, already waited), wait P_j, PV_j, release K/V stage and P buffer.
+    // QK_0, QK_1; then per block j: wait P_j, PV_j into O of group j%2, then QK_{j+2} into
+    // S buffer j%2.  P_j lives in that buffer's first 64 columns; tcgen05.mma instructions of
+    // one thread execute in issue order, so PV_j has read P_j before QK_{j+2} overwrites it.
     if (lane == 0) {
       const uint32_t id_qk = idesc_bf16_f32(kRows, kKeys);
       const uint32_t id_pv = idesc_bf16_f32(kRows, HD) | (1u << 16);  // B (V) MN-major
@@ -209,34 +213,39 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         mma_commit(&s_full[j & 1]);
         return true;
       };
-      ok = qk(0);
+      ok = qk(0) && (nb < 2 || qk(1));
       for (int j = 0; ok && j < nb; ++j) {
-        if (j + 1 < nb && !qk(j + 1)) { ok = false; break; }
         if (!mbar_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u, p.timeout_ns)) { ok = false; break; }
         CF_TTRACE(2, j);
-        tc_fence_after();
         const int s = j % kStages;
         if (!mbar_wait(&kv_full[kStages + s], (uint32_t)(j / kStages) & 1u, p.timeout_ns)) { ok = false; break; }  // V_j
+        tc_fence_after();
         const uint32_t vb = smem_u32(kv_s + s * 2 * kTileBytes + kTileBytes);
-        const uint32_t pa = tmem + kColP + (uint32_t)(j & 1) * 64;
+        const uint32_t pa = tmem + kColS + (uint32_t)(j & 1) * kKeys;
+        const uint32_t od = tmem + kColO + (uint32_t)(j & 1) * HD;
         // V block as the MN-major B operand: 16 keys (two 8-row groups, 1 KB apart) per MMA,
         // head dim in two 64-column atoms 16 KB apart
 #pragma unroll
         for (int kt = 0; kt < kKeys / 16; ++kt)
-          mma_f16_ts(tmem + kColO, pa + (uint32_t)(kt * 8), desc_mnmajor_sw128(vb + kt * 2048, kBoxBytes, 1024),
-                     id_pv, (j > 0 || kt > 0) ? 1u : 0u);
+          mma_f16_ts(od, pa + (uint32_t)(kt * 8), desc_mnmajor_sw128(vb + kt * 2048, kBoxBytes, 1024), id_pv,
+                     (j >= 2 || kt > 0) ? 1u : 0u);
         mma_commit(&kv_empty[kStages + s]);
-        mma_commit(&pv_done[j & 1]);
+        if (j + 2 < nb && !qk(j + 2)) { ok = false; break; }
       }
       mma_commit(o_done);  // also on failure: completes once every issued MMA has finished
     }
     __syncwarp();
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-  } else if (warp < 6) {
-    // ---------------- softmax (warps 2-5, one query row per thread) ----------------
+  } else if (warp >= 2 && warp < kVWarp) {
+    // ---------------- softmax: group g = (warp - 2) / 4 takes blocks j = g, g + 2, ... ----------------
+    // one query row per thread; each group keeps its own running max m, sum l and O (TMEM),
+    // merged at the end
+    const int grp = (warp - 2) >> 2;
     const int qd = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = qd * 32 + lane;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t sa = tmem + lane_base + kColS + (uint32_t)grp * kKeys;  // S_j, then P_j in place
+    const uint32_t oa = tmem + lane_base + kColO + (uint32_t)grp * HD;
     const int qrow = tile * kRows + row;
     const bool valid = qrow < p.rows_total;
     const int rq = valid ? qrow / p.G : 0;
@@ -260,12 +269,21 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       vis1 &= low_bits(p.R, 1);
     }
     float m_used = -INFINITY, l = 0.0f;
-    for (int j = 0; j < nb; ++j) {
-      const int buf = j & 1;
-      if (!mbar_wait_warp(&s_full[buf], (uint32_t)(j >> 1) & 1u, p.timeout_ns)) { ok = false; break; }
+    // a warp whose 32 rows are all past the group (the last row tile) only keeps the
+    // barrier protocol: rows are independent in both products, and O rows past the group
+    // are never written out, so whatever its P rows hold cannot reach a real row
+    const bool warp_live = __any_sync(0xffffffffu, valid);
+    for (int j = grp; j < nb; j += 2) {
+      const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+      // S_j ready; the commit also covers PV_{j-2}, so O of this group is current
+      if (!mbar_wait_warp(&s_full[grp], ph, p.timeout_ns)) { ok = false; break; }
       if (threadIdx.x == 64) CF_TTRACE(3, j);
+      if (!warp_live) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[grp]);
+        continue;
+      }
       tc_fence_after();
-      const uint32_t sa = tmem + lane_base + kColS + (uint32_t)buf * kKeys;
       const bool newblk = j == nc;
       // keep the per-key mask bits from being hoisted out of the block loop (128 live registers)
       asm volatile("" : "+l"(vis0), "+l"(vis1));
@@ -276,116 +294,126 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         if (newblk) return ((col < 64 ? vis0 >> col : vis1 >> (col - 64)) & 1ull) != 0;
         return kbase + col < ctx;
       };
-      // the whole S row into registers: four loads in flight, one wait
-      // (four whole 32-entry arrays: taking the address of part of one array would put
-      // the row in local memory)
-      uint32_t s0[32], s1[32], s2[32], s3[32];
-      tmem_ld_32x32b_x32(sa + 0u, s0);
-      tmem_ld_32x32b_x32(sa + 32u, s1);
-      tmem_ld_32x32b_x32(sa + 64u, s2);
-      tmem_ld_32x32b_x32(sa + 96u, s3);
-      tmem_ld_wait();
-      // key e of the row (e is a compile-time constant wherever this is used)
-      auto sr = [&](int e) -> uint32_t & { return e < 32 ? s0[e] : e < 64 ? s1[e - 32] : e < 96 ? s2[e - 64] : s3[e - 96]; };
-      if (threadIdx.x == 64 && j < 128) { CF_TTRACE(6, 4 * j); }
-      // pass 1: max of the visible raw scores
-      // (masked keys become -inf here, so pass 2 needs no mask: 2^-inf = 0)
-      // (8 partial maxima: a tree instead of one 128-long dependency chain)
-      if (!full) {
-#pragma unroll
-        for (int e = 0; e < kKeys; ++e)
-          if (!visible(e)) sr(e) = __float_as_uint(-INFINITY);
-      }
+      // pass 1: max of the visible raw scores, 64 columns at a time (two loads in flight)
       float mp[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mp[k] = __uint_as_float(sr(k));
+      for (int k = 0; k < 8; ++k) mp[k] = -INFINITY;
 #pragma unroll
-      for (int e = 8; e < kKeys; ++e) mp[e & 7] = fmaxf(mp[e & 7], __uint_as_float(sr(e)));
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t s0[32], s1[32];
+        tmem_ld_32x32b_x32(sa + (uint32_t)(hf * 64), s0);
+        tmem_ld_32x32b_x32(sa + (uint32_t)(hf * 64 + 32), s1);
+        tmem_ld_wait();
+        if (full) {  // the common case: no mask evaluation at all
+#pragma unroll
+          for (int e = 0; e < 64; ++e) mp[e & 7] = fmaxf(mp[e & 7], __uint_as_float(e < 32 ? s0[e] : s1[e - 32]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 64; ++e)
+            if (visible(hf * 64 + e)) mp[e & 7] = fmaxf(mp[e & 7], __uint_as_float(e < 32 ? s0[e] : s1[e - 32]));
+        }
+      }
       const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
                              fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-      // lazy running max: raise it (and rescale l and O) only when this block's max
-      // exceeds it by more than kLazy in log2 units, or it is still -inf
+      // lazy running max: raise it (and rescale l and O) only when this block's max exceeds
+      // it by more than kLazy in log2 units, or it is still -inf
       const float mb = mx * sl;
       const bool need = valid && mb != -INFINITY && (m_used == -INFINITY || mb > m_used + kLazy);
       const float f = need ? (m_used == -INFINITY ? 0.0f : ex2f_approx(m_used - mb)) : 1.0f;
-      bool waited_prev = false;
       if (__any_sync(0xffffffffu, need)) {
         l *= f;
-        if (j > 0) {  // O holds PV_0..PV_{j-1}: wait for PV_{j-1}, then scale this warp's rows
-          if (!mbar_wait_warp(&pv_done[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, p.timeout_ns)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          waited_prev = true;
+        if (j >= 2) {  // O of this group holds PV of its earlier blocks: scale this warp's rows
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
             uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem + lane_base + kColO + (uint32_t)(c * 32), r);
+            tmem_ld_32x32b_x32(oa + (uint32_t)(c * 32), r);
             tmem_ld_wait();
 #pragma unroll
             for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * f);
-            tmem_st_32x32b_x32(tmem + lane_base + kColO + (uint32_t)(c * 32), r);
+            tmem_st_32x32b_x32(oa + (uint32_t)(c * 32), r);
           }
           tmem_st_wait();
         }
         if (need) m_used = mb;
       }
-      // P buffer `buf` was read by PV_{j-2} (implied done when PV_{j-1} was waited)
-      if (j >= 2 && !waited_prev) {
-        if (!mbar_wait_warp(&pv_done[buf], (uint32_t)((j - 2) >> 1) & 1u, p.timeout_ns)) { ok = false; break; }
-        tc_fence_after();
-      }
-      // pass 2: P = 2^(s * scale * log2e - m) as bf16 pairs (keys 2i, 2i+1 per column)
-      const uint32_t pa = tmem + lane_base + kColP + (uint32_t)buf * 64;
       if (threadIdx.x == 64) CF_TTRACE(5, j);
+      // pass 2: P = 2^(s * scale * log2e - m) as bf16 pairs (keys 2i, 2i+1 per column),
+      // written over the first 64 columns of this S buffer: chunk c (keys 32c..32c+31) is
+      // read before columns 16c..16c+15 are written, and later chunks lie above them
       const bool live = m_used != -INFINITY;
       const float nm = live ? -m_used : 0.0f;
-      // 8 partial sums (a tree instead of one long dependency chain)
-      float lp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+      float lp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // partial sums
 #pragma unroll
       for (int c = 0; c < kKeys / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(sa + (uint32_t)(c * 32), r);
+        tmem_ld_wait();
+        if (!full) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (!visible(c * 32 + e)) r[e] = __float_as_uint(-INFINITY);  // 2^-inf = 0
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float p0 = ex2f_approx(fmaf(__uint_as_float(sr(c * 32 + e)), sl, nm));
-          float p1 = ex2f_approx(fmaf(__uint_as_float(sr(c * 32 + e + 1)), sl, nm));
+          float p0 = ex2f_approx(fmaf(__uint_as_float(r[e]), sl, nm));
+          float p1 = ex2f_approx(fmaf(__uint_as_float(r[e + 1]), sl, nm));
           if (!live) p0 = p1 = 0.0f;
           lp[(e >> 1) & 7] += p0 + p1;
           pk[e >> 1] = pack_bf16(p0, p1);
         }
-        tmem_st_32x32b_x16(pa + (uint32_t)(c * 16), pk);
+        tmem_st_32x32b_x16(sa + (uint32_t)(c * 16), pk);
       }
       l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[buf]);
+      if (lane == 0) mbar_arrive(&p_full[grp]);
       if (threadIdx.x == 64) CF_TTRACE(4, j);
     }
-    // ---------------- output: O / l as bf16 ----------------
+    // ---------------- output: merge the two groups, O / l as bf16 ----------------
     if (!mbar_wait_warp(o_done, 0, ok ? p.timeout_ns : kDrainNs)) ok = false;
     tc_fence_after();
+    // every MMA is done, so the Q tile is free: exchange (m, l) per row through it
+    float *ml = reinterpret_cast<float *>(q_s);  // [group][m, l][128 rows]
+    ml[grp * 256 + row] = m_used;
+    ml[grp * 256 + 128 + row] = l;
+    named_bar_sync(1, 8 * 32);  // the 8 softmax warps (all reach it: no early exit above)
+    const float ma = ml[row], la = ml[128 + row], mbb = ml[256 + row], lb = ml[384 + row];
+    const float M = fmaxf(ma, mbb);
+    const float fa = (la > 0.0f && M != -INFINITY) ? ex2f_approx(ma - M) : 0.0f;
+    const float fb = (lb > 0.0f && M != -INFINITY) ? ex2f_approx(mbb - M) : 0.0f;
+    const float L = la * fa + lb * fb;
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
     if (ok) {
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       __nv_bfloat16 *dst = nullptr;
       if (valid) {
         const int g = qrow % p.G;
         dst = p.out + (int64_t)(b * p.R + rq) * p.out_row_stride + (int64_t)(h * p.G + g) * HD;
       }
+      // group g writes head-dim columns [64 g, 64 g + 64) of its rows
+      const uint32_t o0 = tmem + lane_base + kColO, o1 = o0 + HD;
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + kColO + (uint32_t)(c * 32), r);
+      for (int c = 0; c < 2; ++c) {
+        const int col = grp * 64 + c * 32;
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(o0 + (uint32_t)col, ra);
+        tmem_ld_32x32b_x32(o1 + (uint32_t)col, rb);
         tmem_ld_wait();
         if (dst) {
           uint32_t w[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            w[e] = pack_bf16(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv);
+          for (int e = 0; e < 16; ++e) {
+            // a group with no visible key contributes nothing (its O may be unwritten)
+            const float v0 = (fa != 0.0f ? __uint_as_float(ra[2 * e]) * fa : 0.0f) +
+                             (fb != 0.0f ? __uint_as_float(rb[2 * e]) * fb : 0.0f);
+            const float v1 = (fa != 0.0f ? __uint_as_float(ra[2 * e + 1]) * fa : 0.0f) +
+                             (fb != 0.0f ? __uint_as_float(rb[2 * e + 1]) * fb : 0.0f);
+            w[e] = pack_bf16(v0 * inv, v1 * inv);
+          }
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            reinterpret_cast<uint4 *>(dst + c * 32)[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+            reinterpret_cast<uint4 *>(dst + col)[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
         }
       }
     }
@@ -395,7 +423,7 @@ tree_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   if (s_fail) {
     // a wait ran out: let this CTA's own copies land and its MMAs finish (bounded) before
     // TMEM is freed and the CTA exits
-    if (warp == 0 || warp == 6) {
+    if (warp == 0 || warp == kVWarp) {
       for (int jj = max(0, issued - kStages); jj < issued; ++jj)
         mbar_wait_warp(&kv_full[tv * kStages + jj % kStages], (uint32_t)(jj / kStages) & 1u, kDrainNs);
     } else if (warp == 1) {
