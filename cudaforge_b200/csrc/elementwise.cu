@@ -163,17 +163,41 @@ __global__ void silu_mul_kernel(const T *gu, int64_t ldg, T *out, int64_t ldo, i
 template <typename T>
 __device__ __forceinline__ void reduce8(const float *part, int splits, int64_t plane, int64_t off, const T *res,
                                         float (&o)[8]) {
-  float4 a = *reinterpret_cast<const float4 *>(part + off), b = *reinterpret_cast<const float4 *>(part + off + 4);
-  for (int s = 1; s < splits; ++s) {
-    const float4 c = *reinterpret_cast<const float4 *>(part + s * plane + off);
-    const float4 d = *reinterpret_cast<const float4 *>(part + s * plane + off + 4);
-    a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
-    b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
+  float4 a, b;
+  cf::Vec16<T> rv;
+  if (res) rv.raw = *reinterpret_cast<const uint4 *>(res);  // issued with the partial loads
+  if (splits <= 4) {
+    // the fused consumers' case (2-4 splits): every load in flight at once, then the sums
+    // in the order s = 0..splits-1 (the same result as the loop below)
+    float4 pa[4], pb[4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+      if (s < splits) {
+        pa[s] = *reinterpret_cast<const float4 *>(part + s * plane + off);
+        pb[s] = *reinterpret_cast<const float4 *>(part + s * plane + off + 4);
+      }
+    a = pa[0];
+    b = pb[0];
+#pragma unroll
+    for (int s = 1; s < 4; ++s)
+      if (s < splits) {
+        a.x += pa[s].x; a.y += pa[s].y; a.z += pa[s].z; a.w += pa[s].w;
+        b.x += pb[s].x; b.y += pb[s].y; b.z += pb[s].z; b.w += pb[s].w;
+      }
+  } else {
+    a = *reinterpret_cast<const float4 *>(part + off);
+    b = *reinterpret_cast<const float4 *>(part + off + 4);
+    for (int s = 1; s < splits; ++s) {
+      const float4 c = *reinterpret_cast<const float4 *>(part + s * plane + off);
+      const float4 d = *reinterpret_cast<const float4 *>(part + s * plane + off + 4);
+      a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
+      b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
+    }
   }
   o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
   if (res) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] += cf::to_float(res[j]);
+    for (int j = 0; j < 8; ++j) o[j] += rv.get(j);
   }
 }
 
@@ -392,7 +416,8 @@ extern "C" int cf_splitk_rmsnorm(const float *partials, int32_t splits, int32_t 
                                  int64_t ldr, void *y, int64_t ldy, const void *w, void *out, int64_t ldo, float eps,
                                  int32_t dtype, void *stream) {
   if (m < 0 || n <= 0 || n % 8 || splits < 1 || ldy % 8 || ldo % 8 || (residual && ldr % 8)) return CF_EINVAL;
-  if (!partials || !y || !w || !out || !aligned16(partials) || !aligned16(y) || !aligned16(w) || !aligned16(out))
+  if (!partials || !y || !w || !out || !aligned16(partials) || !aligned16(y) || !aligned16(w) || !aligned16(out) ||
+      (residual && !aligned16(residual)))
     return CF_EINVAL;
   if (m == 0) return CF_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
