@@ -152,3 +152,33 @@ def test_verifier_step_raises_on_device_error():
     assert ver.ctx_host == ctx_before  # the failed step committed nothing on the host
     ver.step(dt, dl, u)  # the status word was cleared; the next step runs
     ver.check_status()
+
+
+def test_tree_attention_tcgen05_wait_timeout_and_bad_page():
+    """The tcgen05 path (>= 128 rows per kv head: 65 tree rows x 4 heads): waits driven to
+    expiry record CF_ETIMEOUT and the next call is correct; an invalid page id records
+    CF_ERANGE and leaves the other sequences' outputs untouched."""
+    c = _cache(L=2, Hkv=8, D=128, blocks=300)
+    R, Hq = 65, 32
+    tables, ctx, q, kn, vn, mx = _attn_inputs(c, B=3, R=R, Hq=Hq, ctxs=(300, 1000, 17))
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    kw = dict(rows=R, num_q_heads=Hq, status=st)
+    good = ops.verify_attention(c, 1, q, kn, vn, tables, ctx, mx, **kw).clone()
+    torch.cuda.synchronize()
+    assert st.item() == _lib.CF_OK
+    ops.verify_attention(c, 1, q, kn, vn, tables, ctx, mx, timeout_ns=1, **kw)
+    torch.cuda.synchronize()
+    assert st.item() == _lib.CF_ETIMEOUT
+    st.zero_()
+    again = ops.verify_attention(c, 1, q, kn, vn, tables, ctx, mx, **kw)
+    torch.cuda.synchronize()
+    assert st.item() == _lib.CF_OK
+    assert torch.equal(again, good)
+    bad = tables.clone()
+    bad[1, 5] = c.get_config().total_gpu_blocks + 3  # sequence 1 only
+    out = ops.verify_attention(c, 1, q, kn, vn, bad, ctx, mx, **kw)
+    torch.cuda.synchronize()
+    assert st.item() == _lib.CF_ERANGE
+    rows, ref = out.view(3, R, -1), good.view(3, R, -1)
+    for b in (0, 2):
+        assert torch.equal(rows[b], ref[b])
