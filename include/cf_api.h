@@ -359,6 +359,9 @@ typedef struct cf_kv_layout {
  * (cf_attention_workspace_bytes); num_splits 0 = automatic.
  * A block id outside [0, total_blocks) sets *status = CF_ERANGE and that page
  * reads block 0; an expired pipeline wait sets CF_ETIMEOUT.
+ * bf16, head_dim 128, rows * (num_q_heads / num_kv_heads) >= 128, rows <= 128,
+ * num_splits <= 1 and a 16-byte aligned out: a tcgen05 kernel (S, P and O in
+ * TMEM; no workspace); other shapes: the warp-MMA kernel.
  * ---------------------------------------------------------------------- */
 typedef struct cf_attn_args {
   cf_kv_layout kv;
