@@ -508,7 +508,7 @@ def run_ours(args):
 
 
 # ---------------------------------------------------------------- CPU baseline / reference arm
-def cpu_step_sample(args, threads: int):
+def cpu_step_sample(args, threads: int, parity_out=None):
     """One bounded CPU sample of the verify+accept step at the bench shapes:
     one transformer layer of the 8B-shaped model (torch fp32 on the host,
     weights dequantised from INT4) over the 64 x 6 verify rows with a
@@ -588,10 +588,59 @@ def cpu_step_sample(args, threads: int):
         tokens = int((na + 1).sum())
         kind_acc = "oracle restatement of verify_candidates"
     t_acc = time.perf_counter() - t2
+    if parity_out is not None:  # untimed: the GPU acceptance kernel on this sample's logits
+        parity_out.update(acceptance_parity(args, dl, tl, dt))
     step_s = c.layers * t_layer + t_lm + t_acc
     desc = (f"1 of {c.layers} layers at M={M} rows (ctx {P}) timed and x{c.layers}, + lm_head + acceptance of "
             f"{B} seqs ({kind_acc}); forward is the torch fp32 restatement (the reference has no model forward)")
     return step_s, tokens, desc, {"layer_s": t_layer, "lm_head_s": t_lm, "accept_s": t_acc}
+
+
+def acceptance_parity(args, dl, tl, dt):
+    """Acceptance parity at the bench shape (B sequences, K drafts, the full
+    vocabulary), inside the CPU-baseline leg: the library's GPU acceptance
+    kernel (cf_accept_sample) on the sample's fp32 logits, each sequence's
+    uniforms drawn from the library's mt19937 engine seeded 42 + b (the
+    reference engine's seed for that sequence), its softmax probabilities
+    exported; the reference's compiled verify_candidates (or the oracle
+    restatement when that build is absent) then decides on those same
+    probabilities.  Accepted counts and emitted tokens must agree exactly."""
+    import numpy as np
+
+    import oracle
+    from cudaforge_b200._C import SpeculativeConfig, SpeculativeEngine
+    from cudaforge_b200.accept import accept_sample
+    dev = torch.device("cuda", 0)
+    B, K = dt.shape
+    U = np.stack([_engine_uniforms(SpeculativeConfig, SpeculativeEngine, 42 + b, K + 1, args.temperature)
+                  for b in range(B)])
+    r = accept_sample(torch.from_numpy(np.ascontiguousarray(dl)).to(dev),
+                      torch.from_numpy(np.ascontiguousarray(tl)).to(dev), torch.from_numpy(dt).to(dev),
+                      torch.from_numpy(U).to(dev), temperature=args.temperature, export_probs=True)
+    torch.cuda.synchronize()
+    pd, pt = r.probs_draft.cpu().numpy(), r.probs_target.cpu().numpy()
+    na_gpu = r.num_accepted.cpu().numpy()
+    if oracle.ref_available():
+        kind = "reference verify_candidates (compiled from the reference sources), engine seed 42 + b"
+        res = [oracle.ref_verify(42 + b, dt[b], pd[b], pt[b], -1) for b in range(B)]
+        tok = np.stack([t for t, _, _ in res])
+        na = np.array([n for _, n, _ in res])
+    else:
+        kind = "oracle restatement of verify_candidates on the same uniforms"
+        tok, na, _ = oracle.accept(dt, pd, pt, U, -1)
+    same = [int(na_gpu[b]) == int(na[b]) and r.emitted(b) == tok[b, : int(na[b]) + 1].tolist() for b in range(B)]
+    return {"acceptance": {"sequences": int(B), "k": int(K), "vocab": int(tl.shape[-1]),
+                           "bit_exact_sequences": int(sum(same)), "bit_exact": bool(all(same)),
+                           "mean_accepted": round(float(np.mean(na)), 3), "compared_with": kind},
+            "logits": "not compared in this run: the 8B-width logits vs the fp32 restatement are the "
+                      "GPU test tests/test_cfg3_parity_gpu.py (max-abs and argmax agreement)"}
+
+
+def _engine_uniforms(cfg_cls, eng_cls, seed, n, temperature):
+    cfg = cfg_cls()
+    cfg.rng_seed = seed
+    cfg.temperature = temperature
+    return eng_cls(cfg).draw_uniforms(n)
 
 
 def run_reference(args):
@@ -899,9 +948,11 @@ def main():
     out = run_ours(args)
     if out is not None:
         if out["n_gpus"] == 1 and not args.no_cpu_baseline and args.config == "8b":
-            s, t, desc, parts = cpu_step_sample(args, 1)
+            par = {}
+            s, t, desc, parts = cpu_step_sample(args, 1, parity_out=par)
             out["cpu_baseline"] = {"value": round(t / s, 3), "unit": UNIT, "cores": 1, "kind": "port",
                                    "sample": desc, "parts_s": {k: round(v, 3) for k, v in parts.items()}}
+            out["parity"] = par
         print(json.dumps(out), flush=True)
 
 
