@@ -40,7 +40,9 @@ def test_reference_unit_tests_greedy():
     assert r.num_accepted == 2 and r.accepted_tokens == [1, 2] and r.final_token == 0 and r.end_of_sequence
 
 
-def test_probe_from_the_survey():
+def test_certain_acceptance_then_eos_final_token():
+    """p(draft) = 1 under the target: both drafts accepted; the final draw is the
+    certain token 0, which is the eos id."""
     eng = _C.SpeculativeEngine(_C.SpeculativeConfig())
     r = eng.verify_candidates([1, 2], [[0.2] * 5] * 2, [[0, 1, 0, 0, 0], [0, 0, 1, 0, 0], [1, 0, 0, 0, 0]], 0)
     assert (r.num_accepted, r.accepted_tokens, r.final_token, r.end_of_sequence) == (2, [1, 2], 0, True)
